@@ -1,0 +1,453 @@
+"""Benchmark of the B200 Lloyd iteration (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--impl ours|reference]
+
+A *step* is one Lloyd iteration (assign -> counting-sort update -> finalize)
+over the whole problem of the workload. ``value`` is ms per iteration of the
+whole job (max over ranks, CUDA events, inputs resident in HBM); for N > 1
+the points are sharded over the ranks (strong scaling: fixed total problem)
+with one NCCL all-reduce of sums and counts per iteration.
+
+Workloads (seeded synthetic data of those shapes and
+distributions, generated on the device):
+  c2  B=1  N=131072   K=2048  D=128 fp16, mixture N(0,4I)+N(0,I)
+  c3  B=1  N=524288   K=8192  D=128 fp16, mixture with Zipf(1.1) cluster sizes  [default]
+  c4  B=32 N=16384    K=1024  D=64  bf16, independent mixtures per b (sharded over B)
+  c5  B=1  N=2^24     K=65536 D=128 fp16, iid N(0,1)
+
+Extra keys: ``roofline`` for the assignment kernel (tensor-bound, against the
+measured bf16/fp16 dense peak), ``update`` (HBM-bound, GB/s), ``e2e`` (the same
+metric through ``batch_kmeans_Euclid`` with host-resident inputs copied in and
+results copied out inside the timed region), ``cpu_baseline`` (multi-threaded
+CPU Lloyd loop on a bounded sample, scaled to the whole workload), ``clocks``
+(nvidia-smi samples during the timed region) and ``gpu_launches``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "flash-kmeans-cuda_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+WORKLOADS = {
+    "c2": dict(B=1, N=131072, K=2048, D=128, dtype="float16", data="mixture", zipf=0.0,
+               shard="N", iters=20),
+    "c3": dict(B=1, N=524288, K=8192, D=128, dtype="float16", data="mixture", zipf=1.1,
+               shard="N", iters=10),
+    "c4": dict(B=32, N=16384, K=1024, D=64, dtype="bfloat16", data="mixture", zipf=0.0,
+               shard="B", iters=10),
+    "c5": dict(B=1, N=1 << 24, K=65536, D=128, dtype="float16", data="iid", zipf=0.0,
+               shard="N", iters=5),
+}
+TDT = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
+DT_SHORT = {"float16": "fp16", "bfloat16": "bf16", "float32": "fp32"}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------- data
+def make_data(w: dict, device, seed: int = 0):
+    """Full (B, N, D) points and (B, K, D) initial centroids (seeded subset of the points)."""
+    B, N, K, D = w["B"], w["N"], w["K"], w["D"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    xs = []
+    for b in range(B):
+        if w["data"] == "iid":
+            xb = torch.randn((N, D), generator=g, device=device)
+        else:
+            nc = K
+            centres = 2.0 * torch.randn((nc, D), generator=g, device=device)
+            if w["zipf"] > 0:
+                p = torch.arange(1, nc + 1, device=device, dtype=torch.float64) ** (-w["zipf"])
+                lab = torch.multinomial((p / p.sum()).float(), N, replacement=True, generator=g)
+                lab = torch.randperm(nc, generator=g, device=device)[lab]
+            else:
+                lab = torch.randint(0, nc, (N,), generator=g, device=device)
+            xb = centres[lab]
+            xb.add_(torch.randn((N, D), generator=g, device=device))
+        xs.append(xb.to(TDT[w["dtype"]]))
+        del xb
+    x = torch.stack(xs)
+    del xs
+    init = torch.stack([x[b, torch.randperm(N, generator=g, device=device)[:K]]
+                        for b in range(B)]).contiguous()
+    return x, init
+
+
+# ------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of the bench's GPU during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
+                                     power=float(parts[3]), hw=parts[5], hwt=parts[6],
+                                     swt=parts[7], pcap=parts[8]))
+                except ValueError:
+                    continue
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        loaded = [r for r in rows if r["power"] > 250] or rows
+        reasons = set()
+        for r in loaded:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                            ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[k].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["smax"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+# ---------------------------------------------------------------------- helpers
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(tflops=d["bf16_tflops"], tflops_sustained=d.get("bf16_tflops_sustained"),
+                    hbm=d["hbm_gbs"], src="measured")
+    return dict(tflops=1590.0, tflops_sustained=1400.0, hbm=6650.0, src="fallback")
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per assign launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / f"assign_tc_{workload}.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+def max_over_ranks(v: float, device) -> float:
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return v
+
+
+def barrier_sync(device):
+    torch.cuda.synchronize(device)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+# ------------------------------------------------------------------ CPU timings
+def cpu_sample_rows(w: dict, target_s: float) -> tuple:
+    """Rows of one batch element whose CPU iteration takes ~target_s seconds."""
+    from oracle.cpu_lloyd import time_lloyd_cpu
+
+    n = 4096
+    t = time_lloyd_cpu(1, n, w["K"], w["D"], 1, repeats=1)["seconds"]
+    n2 = int(min(w["N"], max(1024, n * target_s / max(t, 1e-3))))
+    return n2, t * n2 / n
+
+
+def cpu_baseline(w: dict, workload: str) -> dict:
+    from oracle.cpu_lloyd import time_lloyd_cpu
+
+    n_s, _ = cpu_sample_rows(w, target_s=3.0)
+    r = time_lloyd_cpu(1, n_s, w["K"], w["D"], iters=1, repeats=3)
+    scale = (w["B"] * w["N"]) / n_s
+    return {"value": r["ms_per_iter"] * scale, "unit": "ms/iter", "cores": r["threads"],
+            "kind": "port",
+            "sample": (f"{workload}: 1 iteration on {n_s} of {w['B'] * w['N']} points "
+                       f"(full K={w['K']}, D={w['D']}, fp32 CPU PyTorch Lloyd loop, "
+                       f"oracle/cpu_lloyd.py), median of 3, scaled by {scale:.1f}x")}
+
+
+def run_reference_arm(args, w: dict) -> None:
+    """CPU port of the reference loop timed on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.cpu_lloyd import lloyd_cpu
+
+    n_s, _ = cpu_sample_rows(w, target_s=1.0)
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((1, n_s, w["D"]), generator=g)
+    init = x[:, torch.randperm(n_s, generator=g)[:w["K"]]].contiguous()
+    for _ in range(args.warmup):
+        lloyd_cpu(x, init, 1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lloyd_cpu(x, init, 1)
+    dt = time.perf_counter() - t0
+    scale = (w["B"] * w["N"]) / n_s
+    ms = 1e3 * dt / args.steps * scale
+    cores = torch.get_num_threads()
+    line = {
+        "metric": "K-Means ms/iter", "value": ms, "unit": "ms/iter", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "B": w["B"], "N": w["N"], "K": w["K"],
+                   "D": w["D"], "parallelism": "cpu"},
+        "cpu_baseline": {"value": ms, "unit": "ms/iter", "cores": cores, "kind": "port",
+                         "sample": (f"each step: 1 iteration on {n_s} of {w['B'] * w['N']} "
+                                    f"points (full K, D), fp32 CPU PyTorch Lloyd loop "
+                                    f"(oracle/cpu_lloyd.py; the reference has no CPU path), "
+                                    f"scaled by {scale:.1f}x")},
+        "e2e": {"value": ms, "unit": "ms/iter", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- our arm
+def run_ours(args, w: dict) -> None:
+    import flash_kmeans_cuda as fkc
+    from flash_kmeans_cuda import _C, _lib
+    from flash_kmeans_cuda.distributed import batch_kmeans_Euclid_sharded, shard_bounds
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from flash_kmeans_cuda.distributed import init_process_group_from_env
+
+        init_process_group_from_env("nccl", timeout_s=300.0)
+
+    B, N, K, D = w["B"], w["N"], w["K"], w["D"]
+    x_full, init_full = make_data(w, dev, seed=0)
+    if w["shard"] == "N":
+        n0, n1 = shard_bounds(N, world, rank)
+        x = x_full[:, n0:n1].contiguous()
+        init = init_full
+    else:
+        b0, b1 = shard_bounds(B, world, rank)
+        x = x_full[b0:b1].contiguous()
+        init = init_full[b0:b1].contiguous()
+    del x_full
+    torch.cuda.empty_cache()
+    Bl, Nl = x.shape[0], x.shape[1]
+
+    st = LloydState(x, K)
+    cur = init.clone()
+    nxt = torch.empty_like(cur)
+    st.set_centroids(cur)
+    bufs = [cur, nxt]
+
+    def step(i):
+        a, b = bufs[i % 2], bufs[(i + 1) % 2]
+        if w["shard"] == "N" and world > 1:
+            st.local(a)
+            dist.all_reduce(st.sums)
+            dist.all_reduce(st.counts)
+            st.finalize(a, b, False)
+        else:
+            st.step(a, b, False)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier_sync(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.lib.fkc_kernel_launches()
+    with ClockSampler(dev.index) as clk:
+        barrier_sync(dev)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        barrier_sync(dev)
+    launches = int(_lib.lib.fkc_kernel_launches() - launches0)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+
+    # Per-phase timings on the resident data (assign / update / finalize).
+    cur_c = bufs[(args.warmup + args.steps) % 2]   # centroids produced by the last step
+    other = bufs[(args.warmup + args.steps + 1) % 2]
+    reps = 5
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    t_assign = t_update = t_fin = 0.0
+    dims = (Bl, Nl, K, D, st.code, st.ws.data_ptr(), st.ws_bytes)
+    for _ in range(reps + 1):
+        barrier_sync(dev)
+        sp = stream.cuda_stream
+        ev[0].record(stream)
+        _lib.check(_lib.lib.fkc_lloyd_assign(x.data_ptr(), cur_c.data_ptr(), st.ids.data_ptr(),
+                                             st.counts.data_ptr(), *dims, sp), "assign")
+        ev[1].record(stream)
+        _lib.check(_lib.lib.fkc_lloyd_update(x.data_ptr(), st.ids.data_ptr(),
+                                             st.counts.data_ptr(), st.sums.data_ptr(), *dims,
+                                             sp), "update")
+        ev[2].record(stream)
+        _lib.check(_lib.lib.fkc_lloyd_finalize(st.sums.data_ptr(), st.counts.data_ptr(),
+                                               cur_c.data_ptr(), other.data_ptr(), None, *dims,
+                                               sp), "finalize")
+        ev[3].record(stream)
+        torch.cuda.synchronize(dev)
+        if _ == 0:
+            continue  # warm-up rep
+        t_assign += ev[0].elapsed_time(ev[1]) / reps
+        t_update += ev[1].elapsed_time(ev[2]) / reps
+        t_fin += ev[2].elapsed_time(ev[3]) / reps
+    t_assign = max_over_ranks(t_assign, dev)
+    t_update = max_over_ranks(t_update, dev)
+    t_fin = max_over_ranks(t_fin, dev)
+    esz = 2
+    assign_flops = 2.0 * Bl * Nl * K * D
+    update_bytes = Bl * Nl * D * esz + 4 * Bl * Nl + Bl * K * (4 * D + 4)
+    peaks = measured_peaks()
+    tflops = assign_flops / (t_assign * 1e-3) / 1e12
+    traffic = profiled_traffic(args.workload)
+
+    # End-to-end through the public API: host inputs in, host results out.
+    e2e = None
+    if not args.no_e2e:
+        x_host = x.cpu().pin_memory()
+        init_host = init.cpu().pin_memory()
+        iters = w["iters"]
+
+        def e2e_call():
+            xd = x_host.to(dev, non_blocking=True)
+            cd = init_host.to(dev, non_blocking=True)
+            if world == 1:
+                ids, cents, n = fkc.batch_kmeans_Euclid(xd, K, max_iters=iters, tol=0.0,
+                                                        init_centroids=cd)
+            else:
+                ids, cents, n = batch_kmeans_Euclid_sharded(xd, K, max_iters=iters, tol=0.0,
+                                                            init_centroids=cd, shard=w["shard"])
+            ids.to("cpu")
+            cents.to("cpu")
+
+        e2e_call()
+        barrier_sync(dev)
+        reps_e2e = 2
+        t0 = time.perf_counter()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(reps_e2e):
+            e2e_call()
+        f1.record(stream)
+        barrier_sync(dev)
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1) / (reps_e2e * iters), dev)
+        h2d = (x_host.numel() * x_host.element_size() + init_host.numel() *
+               init_host.element_size())
+        d2h = Bl * Nl * 4 + init.numel() * init.element_size()
+        e2e = {"value": e2e_ms, "unit": "ms/iter",
+               "h2d_bytes_per_step": h2d / iters, "d2h_bytes_per_step": d2h / iters,
+               "note": (f"one batch_kmeans_Euclid call of {iters} iterations per "
+                        f"{iters} steps: pinned-host x + init copied in, labels + "
+                        f"centroids copied out, inside the timed region")}
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_baseline(w, args.workload)
+            except Exception as e:  # pragma: no cover
+                cpu = {"value": None, "error": str(e)}
+        line = {
+            "metric": "K-Means ms/iter", "value": ms, "unit": "ms/iter", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": DT_SHORT[w["dtype"]], "data": "synthetic",
+            "config": {"workload": args.workload, "B": B, "N": N, "K": K, "D": D,
+                       "parallelism": f"dp{world}-shard{w['shard']}",
+                       "l2": (f"x ({B * N * D * esz / 1e6:.0f} MB) > L2 (126 MB): no flush"
+                              if B * N * D * esz > L2_BYTES else "x fits in L2")},
+            "assign_tflops": tflops,
+            "assign_ms": t_assign, "update_ms": t_update, "finalize_ms": t_fin,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["tflops"],
+                         "unit": "TFLOP/s", "frac": tflops / peaks["tflops"],
+                         "traffic": traffic, "kernel": "assign_tc_kernel",
+                         "peak_src": f"{peaks['src']} bf16 dense burst (fp16 dense is equal)"},
+            "update": {"bound": "hbm", "achieved_gbs": update_bytes / (t_update * 1e-3) / 1e9,
+                       "peak_gbs": peaks["hbm"],
+                       "frac": update_bytes / (t_update * 1e-3) / 1e9 / peaks["hbm"],
+                       "algorithmic_bytes": update_bytes},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warmup raised to 3 (minimum)")
+        args.warmup = 3
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference_arm(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,432 @@
+// extern "C" entry points of libfkc_b200.so (declared in include/fkc_capi.h),
+// plus the host-side services the launchers share: per-thread error text,
+// per-device property cache, TMA descriptor encoding and the device error word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <array>
+#include <atomic>
+#include <cstdarg>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "fkc_internal.h"
+
+// Written (atomicCAS from 0) by kernels whose bounded pipeline waits expired.
+__device__ int g_fkc_device_error = 0;
+
+namespace fkc {
+namespace {
+
+thread_local char g_last_error[1024] = {0};
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+std::array<DeviceInfo, kMaxDevices> g_dev_info{};
+std::array<bool, kMaxDevices> g_dev_ready{};
+std::array<int*, kMaxDevices> g_err_word{};
+std::atomic<uint64_t> g_launches{0};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool env_flag(const char* name) {
+  const char* s = std::getenv(name);
+  return s != nullptr && (std::strcmp(s, "1") == 0 || std::strcmp(s, "true") == 0);
+}
+
+// FKC_ASSIGN_FORCE_SAFE=1 routes every assignment to the CUDA-core kernel
+// (reference: flash_kmeans_cuda/csrc/api.cpp:12-19, read once).
+bool force_safe_path() {
+  static const bool v = env_flag("FKC_ASSIGN_FORCE_SAFE");
+  return v;
+}
+
+}  // namespace
+
+int set_error(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n)); }
+
+int current_device_info(const DeviceInfo** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(FKC_EUNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kMaxDevices) return set_error(FKC_EUNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_dev_ready[dev]) {
+    DeviceInfo di;
+    di.device = dev;
+    FKC_CUDA_TRY(cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev));
+    FKC_CUDA_TRY(cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, dev));
+    FKC_CUDA_TRY(cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, dev));
+    int smem = 0;
+    FKC_CUDA_TRY(cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    di.smem_optin = static_cast<size_t>(smem);
+    g_dev_info[dev] = di;
+    g_dev_ready[dev] = true;
+  }
+  *out = &g_dev_info[dev];
+  return FKC_OK;
+}
+
+int* device_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_err_word[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fkc_device_error) != cudaSuccess) return nullptr;
+    g_err_word[dev] = static_cast<int*>(p);
+  }
+  return g_err_word[dev];
+}
+
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0,
+                   uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                   uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    cudaGetLastError();
+  });
+  if (g_encode == nullptr)
+    return set_error(FKC_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {dim0, dim1, dim2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  const cuuint32_t elem_strides[3] = {1, 1, 1};
+  const CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box,
+                              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FKC_ECUDA,
+                     "cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu} box {%u,%u}",
+                     static_cast<int>(r), static_cast<unsigned long long>(dim0),
+                     static_cast<unsigned long long>(dim1), static_cast<unsigned long long>(dim2),
+                     box0, box1);
+  return FKC_OK;
+}
+
+namespace {
+
+// Shape/dtype eligibility of the tensor-core assignment, independent of the
+// device (workspace sizes must not depend on which GPU is current).
+bool tc_shape_ok(int64_t D, int dtype) {
+  return (dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 256 &&
+         D % 16 == 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool use_tc(const void* x, const void* c, int64_t D, int dtype) {
+  return tc_shape_ok(D, dtype) && !force_safe_path() && aligned16(x) && aligned16(c) &&
+         assign_tc_supported(D, dtype);
+}
+
+int check_dims(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
+  FKC_REQUIRE(dtype_valid(dtype), "dtype must be FKC_DTYPE_F16/BF16/F32 (got %d)", dtype);
+  FKC_REQUIRE(B >= 1 && N >= 1 && K >= 1 && D >= 1,
+              "B, N, K, D must be >= 1 (got B=%lld N=%lld K=%lld D=%lld)",
+              static_cast<long long>(B), static_cast<long long>(N), static_cast<long long>(K),
+              static_cast<long long>(D));
+  FKC_REQUIRE(N <= 2147483647ll && K <= 2147483647ll && D <= 65536,
+              "N and K must fit int32 and D <= 65536");
+  FKC_REQUIRE(B <= (1ll << 31) / 1 && B * K <= (1ll << 31) - 1,
+              "B*K must be < 2^31 (got %lld)", static_cast<long long>(B * K));
+  return FKC_OK;
+}
+
+cudaStream_t as_stream(fkc_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+size_t assign_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
+  if (!tc_shape_ok(D, dtype)) return 0;
+  return align_up(static_cast<size_t>(B * N) * 32, 256) +
+         align_up(static_cast<size_t>(B * K) * 32, 256);
+}
+
+struct LloydWs {
+  uint8_t* aext = nullptr;  // (B,N,16) bf16, tensor-core path
+  uint8_t* cext = nullptr;  // (B,K,16) bf16, tensor-core path
+  float* c_sq = nullptr;    // (B,K) fp32
+  UpdateWorkspace upd{};
+};
+
+size_t lloyd_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
+  return assign_ws_bytes(B, N, K, D, dtype) + align_up(static_cast<size_t>(B * K) * 4, 256) +
+         update_workspace_bytes(B, N, K);
+}
+
+int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                LloydWs* out) {
+  const size_t need = lloyd_ws_bytes(B, N, K, D, dtype);
+  if (ws == nullptr || ws_bytes < need)
+    return set_error(FKC_EWORKSPACE, "Lloyd workspace needs %zu bytes (got %zu at %p)", need,
+                     ws_bytes, ws);
+  FKC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255u) == 0,
+              "workspace must be 256-byte aligned");
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  if (tc_shape_ok(D, dtype)) {
+    out->aext = p;
+    p += align_up(static_cast<size_t>(B * N) * 32, 256);
+    out->cext = p;
+    p += align_up(static_cast<size_t>(B * K) * 32, 256);
+  }
+  out->c_sq = reinterpret_cast<float*>(p);
+  p += align_up(static_cast<size_t>(B * K) * 4, 256);
+  out->upd = carve_update_workspace(p, B, N, K);
+  return FKC_OK;
+}
+
+int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* counts,
+                    bool counts_ready, const UpdateWorkspace& uw, int64_t B, int64_t N,
+                    int64_t K, int64_t D, int dtype, cudaStream_t st) {
+  if (!counts_ready) {
+    FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
+    FKC_TRY(launch_histogram(ids, counts, B, N, K, st));
+  }
+  FKC_TRY(launch_counting_sort(ids, counts, uw, B, N, K, st));
+  FKC_CUDA_TRY(cudaMemsetAsync(sums, 0, static_cast<size_t>(B * K * D) * 4, st));
+  return launch_run_accumulate(x, uw.perm, uw.ids_sorted, sums, nullptr, B, N, K, D, dtype, st);
+}
+
+}  // namespace
+}  // namespace fkc
+
+using namespace fkc;
+
+extern "C" {
+
+FKC_CAPI_EXPORT int fkc_abi_version(void) { return 1; }
+
+FKC_CAPI_EXPORT uint64_t fkc_kernel_launches(void) { return g_launches.load(); }
+
+FKC_CAPI_EXPORT const char* fkc_last_error(void) { return g_last_error; }
+
+FKC_CAPI_EXPORT const char* fkc_status_string(int status) {
+  switch (status) {
+    case FKC_OK: return "FKC_OK";
+    case FKC_EINVAL: return "FKC_EINVAL";
+    case FKC_ECUDA: return "FKC_ECUDA";
+    case FKC_EUNSUPPORTED: return "FKC_EUNSUPPORTED";
+    case FKC_ETIMEOUT: return "FKC_ETIMEOUT";
+    case FKC_EWORKSPACE: return "FKC_EWORKSPACE";
+    default: return "FKC_E?";
+  }
+}
+
+FKC_CAPI_EXPORT int fkc_device_supported(void) {
+  const DeviceInfo* di = nullptr;
+  if (current_device_info(&di) != FKC_OK) return 0;
+  return di->cc_major == 10 ? 1 : 0;
+}
+
+FKC_CAPI_EXPORT int fkc_device_status(void) {
+  clear_error();
+  FKC_CUDA_TRY(cudaDeviceSynchronize());
+  int v = 0;
+  FKC_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_fkc_device_error, sizeof(int)));
+  if (v != 0) {
+    const int zero = 0;
+    FKC_CUDA_TRY(cudaMemcpyToSymbol(g_fkc_device_error, &zero, sizeof(int)));
+    return set_error(FKC_ETIMEOUT, "a device pipeline wait expired (site code %d)", v);
+  }
+  return FKC_OK;
+}
+
+FKC_CAPI_EXPORT size_t fkc_assign_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
+                                                 int dtype) {
+  if (B < 1 || N < 1 || K < 1 || D < 1) return 0;
+  return assign_ws_bytes(B, N, K, D, dtype);
+}
+
+FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float* x_sq,
+                               const float* c_sq, int32_t* ids, int64_t B, int64_t N, int64_t K,
+                               int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                               fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x != nullptr && centroids != nullptr && ids != nullptr,
+              "x, centroids and cluster_ids must be non-null");
+  const cudaStream_t st = as_stream(stream);
+  if (use_tc(x, centroids, D, dtype)) {
+    const size_t need = assign_ws_bytes(B, N, K, D, dtype);
+    if (workspace == nullptr || workspace_bytes < need)
+      return set_error(FKC_EWORKSPACE, "assign workspace needs %zu bytes (got %zu)", need,
+                       workspace_bytes);
+    FKC_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+                "workspace must be 256-byte aligned");
+    uint8_t* aext = static_cast<uint8_t*>(workspace);
+    uint8_t* cext = aext + align_up(static_cast<size_t>(B * N) * 32, 256);
+    FKC_TRY(launch_xnorm_ext(x, aext, B, N, D, dtype, st));
+    FKC_TRY(launch_cnorm_ext(centroids, c_sq, cext, nullptr, B, K, D, dtype, st));
+    return launch_assign_tc(x, centroids, aext, cext, ids, nullptr, B, N, K, D, dtype, st);
+  }
+  return launch_assign_simt(x, centroids, x_sq, c_sq, ids, B, N, K, D, dtype, st);
+}
+
+FKC_CAPI_EXPORT int fkc_update_sorted(const void* x_sorted, const int32_t* ids_sorted,
+                                      float* sums, int32_t* counts, int64_t B, int64_t N,
+                                      int64_t K, int64_t D, int dtype, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x_sorted && ids_sorted && sums && counts, "null argument");
+  return launch_run_accumulate(x_sorted, nullptr, ids_sorted, sums, counts, B, N, K, D, dtype,
+                               as_stream(stream));
+}
+
+FKC_CAPI_EXPORT int fkc_update_sorted_indexed(const void* x, const int32_t* sorted_idx,
+                                              const int32_t* ids_sorted, float* sums,
+                                              int32_t* counts, int64_t B, int64_t N, int64_t K,
+                                              int64_t D, int dtype, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x && sorted_idx && ids_sorted && sums && counts, "null argument");
+  return launch_run_accumulate(x, sorted_idx, ids_sorted, sums, counts, B, N, K, D, dtype,
+                               as_stream(stream));
+}
+
+FKC_CAPI_EXPORT size_t fkc_update_workspace_size(int64_t B, int64_t N, int64_t K) {
+  if (B < 1 || N < 1 || K < 1) return 0;
+  return update_workspace_bytes(B, N, K);
+}
+
+FKC_CAPI_EXPORT int fkc_update(const void* x, const int32_t* ids, float* sums, int32_t* counts,
+                               int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                               void* workspace, size_t workspace_bytes, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x && ids && sums && counts, "null argument");
+  const size_t need = update_workspace_bytes(B, N, K);
+  if (workspace == nullptr || workspace_bytes < need)
+    return set_error(FKC_EWORKSPACE, "update workspace needs %zu bytes (got %zu)", need,
+                     workspace_bytes);
+  const UpdateWorkspace uw = carve_update_workspace(workspace, B, N, K);
+  return update_from_ids(x, ids, sums, counts, false, uw, B, N, K, D, dtype, as_stream(stream));
+}
+
+FKC_CAPI_EXPORT int fkc_finalize(const float* sums, const int32_t* counts, const void* old_c,
+                                 void* new_c, float* c_sq_out, float* shift_out, int64_t B,
+                                 int64_t K, int64_t D, int dtype, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, 1, K, D, dtype));
+  FKC_REQUIRE(sums && counts && old_c && new_c, "null argument");
+  return launch_finalize(sums, counts, old_c, new_c, c_sq_out, nullptr, shift_out, B, K, D,
+                         dtype, as_stream(stream));
+}
+
+FKC_CAPI_EXPORT size_t fkc_lloyd_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
+                                                int dtype) {
+  if (B < 1 || N < 1 || K < 1 || D < 1) return 0;
+  return lloyd_ws_bytes(B, N, K, D, dtype);
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_prepare(const void* x, int64_t B, int64_t N, int64_t K, int64_t D,
+                                      int dtype, void* workspace, size_t workspace_bytes,
+                                      fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x != nullptr, "x must be non-null");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  if (w.aext != nullptr) FKC_TRY(launch_xnorm_ext(x, w.aext, B, N, D, dtype, as_stream(stream)));
+  return FKC_OK;
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_set_centroids(const void* centroids, int64_t B, int64_t N,
+                                            int64_t K, int64_t D, int dtype, void* workspace,
+                                            size_t workspace_bytes, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(centroids != nullptr, "centroids must be non-null");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  return launch_cnorm_ext(centroids, nullptr, w.cext, w.c_sq, B, K, D, dtype, as_stream(stream));
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32_t* ids,
+                                     int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
+                                     int dtype, void* workspace, size_t workspace_bytes,
+                                     fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x && centroids && ids && counts, "null argument");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  const cudaStream_t st = as_stream(stream);
+  FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
+  if (w.aext != nullptr && use_tc(x, centroids, D, dtype))
+    return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, B, N, K, D, dtype, st);
+  FKC_TRY(launch_assign_simt(x, centroids, nullptr, w.c_sq, ids, B, N, K, D, dtype, st));
+  return launch_histogram(ids, counts, B, N, K, st);
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_update(const void* x, const int32_t* ids, const int32_t* counts,
+                                     float* sums, int64_t B, int64_t N, int64_t K, int64_t D,
+                                     int dtype, void* workspace, size_t workspace_bytes,
+                                     fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x && ids && counts && sums, "null argument");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  return update_from_ids(x, ids, sums, const_cast<int32_t*>(counts), true, w.upd, B, N, K, D,
+                         dtype, as_stream(stream));
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_local(const void* x, const void* centroids, int32_t* ids,
+                                    float* sums, int32_t* counts, int64_t B, int64_t N,
+                                    int64_t K, int64_t D, int dtype, void* workspace,
+                                    size_t workspace_bytes, fkc_stream_t stream) {
+  FKC_TRY(fkc_lloyd_assign(x, centroids, ids, counts, B, N, K, D, dtype, workspace,
+                           workspace_bytes, stream));
+  return fkc_lloyd_update(x, ids, counts, sums, B, N, K, D, dtype, workspace, workspace_bytes,
+                          stream);
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_finalize(const float* sums, const int32_t* counts,
+                                       const void* old_c, void* new_c, float* shift_out,
+                                       int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                                       void* workspace, size_t workspace_bytes,
+                                       fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(sums && counts && old_c && new_c, "null argument");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  return launch_finalize(sums, counts, old_c, new_c, w.c_sq, w.cext, shift_out, B, K, D, dtype,
+                         as_stream(stream));
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c, int32_t* ids,
+                                   float* sums, int32_t* counts, float* shift_out, int64_t B,
+                                   int64_t N, int64_t K, int64_t D, int dtype, void* workspace,
+                                   size_t workspace_bytes, fkc_stream_t stream) {
+  FKC_TRY(fkc_lloyd_local(x, old_c, ids, sums, counts, B, N, K, D, dtype, workspace,
+                          workspace_bytes, stream));
+  return fkc_lloyd_finalize(sums, counts, old_c, new_c, shift_out, B, N, K, D, dtype, workspace,
+                            workspace_bytes, stream);
+}
+
+}  // extern "C"

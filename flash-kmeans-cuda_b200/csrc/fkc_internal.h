@@ -1,0 +1,120 @@
+// Host-side internals shared by the translation units of libfkc_b200.so:
+// status/error reporting, per-device properties, TMA descriptor encoding and
+// the launcher entry points the C-ABI dispatches to.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/fkc_capi.h"
+
+namespace fkc {
+
+// Records a formatted message for fkc_last_error() and returns `status`.
+int set_error(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void clear_error();
+
+#define FKC_REQUIRE(cond, ...)                                                  \
+  do {                                                                          \
+    if (!(cond)) return ::fkc::set_error(FKC_EINVAL, __VA_ARGS__);              \
+  } while (0)
+
+#define FKC_CUDA_TRY(expr)                                                      \
+  do {                                                                          \
+    cudaError_t fkc_e_ = (expr);                                                \
+    if (fkc_e_ != cudaSuccess)                                                  \
+      return ::fkc::set_error(FKC_ECUDA, "%s failed: %s (%s:%d)", #expr,        \
+                              cudaGetErrorString(fkc_e_), __FILE__, __LINE__); \
+  } while (0)
+
+#define FKC_TRY(expr)                                                           \
+  do {                                                                          \
+    int fkc_s_ = (expr);                                                        \
+    if (fkc_s_ != FKC_OK) return fkc_s_;                                        \
+  } while (0)
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+  size_t smem_optin = 0;
+};
+
+// Cached per device (queried once; the reference re-queried on every call).
+int current_device_info(const DeviceInfo** out);
+
+// 3-D tiled tensor map {dim0 (contiguous), dim1, dim2} for a row-major array.
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                   uint64_t dim0, uint64_t dim1, uint64_t dim2, uint64_t stride1_bytes,
+                   uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+                   CUtensorMapSwizzle swizzle);
+
+inline size_t dtype_size(int dtype) { return dtype == FKC_DTYPE_F32 ? 4 : 2; }
+inline bool dtype_valid(int dtype) {
+  return dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16 || dtype == FKC_DTYPE_F32;
+}
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device-resident error word written by kernels whose bounded waits expired.
+int* device_error_word();
+
+// Counts kernels launched by this library (reported by fkc_kernel_launches()).
+void count_launches(int n);
+
+// ----------------------------------------------------------------------------
+// Launchers (each validates what is specific to it and launches on `stream`).
+// ----------------------------------------------------------------------------
+
+// True when the tcgen05 assignment kernel handles this shape/dtype on the
+// current device.
+bool assign_tc_supported(int64_t D, int dtype);
+
+// Row-norm extension rows for the tcgen05 path: aext[b,n,:] = {h1,h2,h3,1,1,1,0...}
+// with h1+h2+h3 = -0.5*||x[b,n]||^2 split over three bf16 values.
+int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D, int dtype,
+                     cudaStream_t stream);
+// Centroid terms: extension rows cext[b,k,:] = {1,1,1,h1,h2,h3,0...} with
+// h = -0.5*c_sq (cext nullable) and/or c_sq_out[b,k] (nullable). c_sq is taken
+// from `c_sq` when non-null, otherwise computed from the centroids.
+int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
+                     int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream);
+
+int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
+                     int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
+                     int dtype, cudaStream_t stream);
+
+int launch_assign_simt(const void* x, const void* centroids, const float* x_sq,
+                       const float* c_sq, int32_t* ids, int64_t B, int64_t N, int64_t K,
+                       int64_t D, int dtype, cudaStream_t stream);
+
+// Update: counting sort of labels + permutation-driven gather-accumulate.
+struct UpdateWorkspace {
+  int32_t* offsets;     // (B, K) exclusive prefix of counts
+  int32_t* cursor;      // (B, K) scatter cursors
+  int32_t* perm;        // (B, N) row index in cluster order
+  int32_t* ids_sorted;  // (B, N) label in cluster order
+};
+size_t update_workspace_bytes(int64_t B, int64_t N, int64_t K);
+UpdateWorkspace carve_update_workspace(void* ws, int64_t B, int64_t N, int64_t K);
+
+int launch_histogram(const int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K,
+                     cudaStream_t stream);
+int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
+                         int64_t B, int64_t N, int64_t K, cudaStream_t stream);
+// sums[b, ids_sorted[i], :] += x[b, perm ? perm[i] : i, :] over sorted runs.
+// counts (nullable) += run lengths. sums/counts must be initialised by the caller.
+int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids_sorted,
+                          float* sums, int32_t* counts, int64_t B, int64_t N, int64_t K,
+                          int64_t D, int dtype, cudaStream_t stream);
+
+int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
+                    float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,
+                    int64_t D, int dtype, cudaStream_t stream);
+
+}  // namespace fkc

@@ -1,0 +1,195 @@
+/*
+ * fkc_capi.h - C-ABI of libfkc_b200.so, the B200 (sm_100a) implementation of
+ * the batched Euclidean K-Means Lloyd iteration of flash-kmeans-cuda.
+ *
+ * Plain pointers and sizes only: no torch or C++ types cross this boundary.
+ * Every entry point
+ *   - validates its arguments on the host and returns FKC_OK (0) or a
+ *     negative FKC_E* status; fkc_last_error() then returns a message for the
+ *     calling thread (the counterpart of the reference's TORCH_CHECK text);
+ *   - launches asynchronously on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) on the CURRENT CUDA device, and never synchronises;
+ *   - takes device pointers; dense row-major layouts as documented per call.
+ *
+ * Element types: FKC_DTYPE_F16 / FKC_DTYPE_BF16 / FKC_DTYPE_F32 select the
+ * type of x and of the centroids. Sums are always fp32, labels and counts
+ * int32, as in the reference.
+ *
+ * Reference interfaces replaced (paths inside OpsiClear/flash-kmeans-cuda):
+ *   flash_kmeans_cuda/csrc/bindings.cpp:43-102  (_C.euclid_assign, _C.centroid_update_sorted,
+ *                                                _C.centroid_update_sorted_indexed,
+ *                                                _C.centroid_finalize)
+ *   flash_kmeans_cuda/csrc/api.cpp:47-113       (fkc:: libtorch API)
+ *   flash_kmeans_cuda/csrc/assign/assign.h:32-44, csrc/update/update.h:28-63 (launchers)
+ *   flash_kmeans_cuda/ops.py:58-112, kmeans.py:73-105 (sort/route and iteration glue)
+ */
+#ifndef FKC_CAPI_H_
+#define FKC_CAPI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32)
+#define FKC_CAPI_EXPORT __declspec(dllexport)
+#else
+#define FKC_CAPI_EXPORT __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; declared here so the header needs no CUDA include. */
+typedef struct CUstream_st* fkc_stream_t;
+
+enum {
+  FKC_OK = 0,
+  FKC_EINVAL = -1,        /* bad argument: shape, dtype, null or misaligned pointer */
+  FKC_ECUDA = -2,         /* CUDA runtime/driver call failed (launch, attribute, tensor map) */
+  FKC_EUNSUPPORTED = -3,  /* no CUDA device / device is not sm_100 */
+  FKC_ETIMEOUT = -4,      /* a bounded device-side pipeline wait expired (see fkc_device_status) */
+  FKC_EWORKSPACE = -5     /* workspace missing or smaller than *_workspace_size() */
+};
+
+enum { FKC_DTYPE_F16 = 0, FKC_DTYPE_BF16 = 1, FKC_DTYPE_F32 = 2 };
+
+/* ABI revision of this header (bumped on incompatible change). */
+FKC_CAPI_EXPORT int fkc_abi_version(void);
+
+/* Message describing the last failing call on this thread ("" if none). */
+FKC_CAPI_EXPORT const char* fkc_last_error(void);
+
+/* Name of a status code. */
+FKC_CAPI_EXPORT const char* fkc_status_string(int status);
+
+/* 1 when the current device runs the tcgen05 kernels (sm_100), else 0. */
+FKC_CAPI_EXPORT int fkc_device_supported(void);
+
+/* Number of CUDA kernels this library has launched in this process. */
+FKC_CAPI_EXPORT uint64_t fkc_kernel_launches(void);
+
+/* Synchronises the current device and returns FKC_OK, or FKC_ETIMEOUT if a
+ * kernel of this library recorded an expired pipeline wait since the last
+ * call (the record is cleared). Use in tests and health checks. */
+FKC_CAPI_EXPORT int fkc_device_status(void);
+
+/* ------------------------------------------------------------------------
+ * Assignment
+ *   ids[b,n] = argmin_k ||x[b,n,:] - c[b,k,:]||^2, ties -> lowest k.
+ *   x (B,N,D), centroids (B,K,D) of `dtype`; ids (B,N) int32.
+ *   c_sq (B,K) fp32 = ||c||^2 or NULL (computed). x_sq (B,N) fp32 or NULL:
+ *   read only by the fp32 / odd-D fallback, which clamps distances at 0 as
+ *   the reference's safe kernel does; the tensor-core path ignores it (as the
+ *   reference's raw-distance mma path does).
+ *   fp16/bf16 with D % 16 == 0 and D <= 256 run the tcgen05 kernel.
+ * Replaces: _C.euclid_assign (csrc/bindings.cpp:43-71),
+ *           fkc::euclid_assign_out (csrc/api.cpp:58-72),
+ *           launch_assign_sm80 / launch_assign_safe (csrc/assign/assign.h:32-44).
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT size_t fkc_assign_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
+                                                 int dtype);
+FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float* x_sq,
+                               const float* c_sq, int32_t* ids, int64_t B, int64_t N, int64_t K,
+                               int64_t D, int dtype, void* workspace, size_t workspace_bytes,
+                               fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Sorted-run accumulators with the reference _C semantics: they ADD into
+ * caller-initialised sums (B,K,D) fp32 and counts (B,K) int32.
+ *   ids_sorted (B,N): labels sorted ascending along N.
+ *   fkc_update_sorted:          rows read from x_sorted (B,N,D).
+ *   fkc_update_sorted_indexed:  rows read from x[b, sorted_idx[b,i], :].
+ * Labels outside [0,K) are skipped (reference: update_sorted.cu:94).
+ * Replaces: _C.centroid_update_sorted (csrc/bindings.cpp:73-80),
+ *           _C.centroid_update_sorted_indexed (csrc/bindings.cpp:82-90),
+ *           csrc/update/update.h:28-48.
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT int fkc_update_sorted(const void* x_sorted, const int32_t* ids_sorted,
+                                      float* sums, int32_t* counts, int64_t B, int64_t N,
+                                      int64_t K, int64_t D, int dtype, fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_update_sorted_indexed(const void* x, const int32_t* sorted_idx,
+                                              const int32_t* ids_sorted, float* sums,
+                                              int32_t* counts, int64_t B, int64_t N, int64_t K,
+                                              int64_t D, int dtype, fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Centroid update from UNSORTED labels: counting sort of ids (histogram,
+ * scan, scatter of a permutation) then a permutation-driven gather-accumulate.
+ * Writes sums (B,K,D) fp32 and counts (B,K) int32 completely (no pre-zeroing).
+ * Labels must lie in [0,K).
+ * Replaces: ops.centroid_update_sorted (flash_kmeans_cuda/ops.py:58-112),
+ *           i.e. torch.sort + zero_ + _C.centroid_update_sorted[_indexed].
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT size_t fkc_update_workspace_size(int64_t B, int64_t N, int64_t K);
+FKC_CAPI_EXPORT int fkc_update(const void* x, const int32_t* ids, float* sums, int32_t* counts,
+                               int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                               void* workspace, size_t workspace_bytes, fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Finalize: new[b,k,:] = counts[b,k] > 0 ? dtype(sums[b,k,:] / counts[b,k])
+ *                                        : old[b,k,:]
+ * Optional outputs (NULL to skip):
+ *   c_sq_out (B,K) fp32: ||new[b,k]||^2 of the dtype-rounded centroids
+ *                        (reference computes it next iteration, kmeans.py:94);
+ *   shift_out (1) fp32:  max_{b,k} ||new - old||_2 (kmeans.py:102-104).
+ * new_c may alias old_c (in-place update; each element is read before it is
+ * written by the same thread).
+ * Replaces: _C.centroid_finalize (csrc/bindings.cpp:92-102),
+ *           fkc::centroid_finalize_out (csrc/api.cpp:105-113).
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT int fkc_finalize(const float* sums, const int32_t* counts, const void* old_c,
+                                 void* new_c, float* c_sq_out, float* shift_out, int64_t B,
+                                 int64_t K, int64_t D, int dtype, fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Lloyd iteration (kmeans.py:73-105 as device-resident steps). One workspace
+ * of fkc_lloyd_workspace_size() bytes carries state between the calls:
+ *   fkc_lloyd_prepare   once per x: per-row terms of the assignment.
+ *   fkc_lloyd_assign    labels ids (B,N) and per-cluster counts (B,K) (the
+ *                       histogram is fused into the assignment kernel);
+ *   fkc_lloyd_update    sums (B,K,D) fp32 from x, ids and those counts;
+ *   fkc_lloyd_local     assign + update of this rank's x.
+ *                       Multi-GPU callers all-reduce sums/counts here.
+ *   fkc_lloyd_finalize  new centroids (+ shift_out if non-NULL) from the
+ *                       (reduced) sums/counts; also prepares the next
+ *                       iteration's centroid terms inside the workspace.
+ *   fkc_lloyd_iter      local + finalize.
+ * The centroids passed to fkc_lloyd_local must be those last produced by
+ * fkc_lloyd_finalize with the same workspace, or fkc_lloyd_set_centroids
+ * must be called first (initial centroids).
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT size_t fkc_lloyd_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
+                                                int dtype);
+FKC_CAPI_EXPORT int fkc_lloyd_prepare(const void* x, int64_t B, int64_t N, int64_t K, int64_t D,
+                                      int dtype, void* workspace, size_t workspace_bytes,
+                                      fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_set_centroids(const void* centroids, int64_t B, int64_t N,
+                                            int64_t K, int64_t D, int dtype, void* workspace,
+                                            size_t workspace_bytes, fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32_t* ids,
+                                     int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
+                                     int dtype, void* workspace, size_t workspace_bytes,
+                                     fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_update(const void* x, const int32_t* ids, const int32_t* counts,
+                                     float* sums, int64_t B, int64_t N, int64_t K, int64_t D,
+                                     int dtype, void* workspace, size_t workspace_bytes,
+                                     fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_local(const void* x, const void* centroids, int32_t* ids,
+                                    float* sums, int32_t* counts, int64_t B, int64_t N,
+                                    int64_t K, int64_t D, int dtype, void* workspace,
+                                    size_t workspace_bytes, fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_finalize(const float* sums, const int32_t* counts,
+                                       const void* old_c, void* new_c, float* shift_out,
+                                       int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                                       void* workspace, size_t workspace_bytes,
+                                       fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c, int32_t* ids,
+                                   float* sums, int32_t* counts, float* shift_out, int64_t B,
+                                   int64_t N, int64_t K, int64_t D, int dtype, void* workspace,
+                                   size_t workspace_bytes, fkc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FKC_CAPI_H_ */

@@ -1,0 +1,96 @@
+"""CPU tests of the C-ABI boundary: libfkc_b200.so loads, exports every function
+declared in include/fkc_capi.h, and rejects bad arguments on the host with the
+documented status codes before touching a GPU."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "fkc_capi.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"FKC_CAPI_EXPORT\s+[\w\s\*]+?\b(fkc_\w+)\s*\(", text))
+
+
+def test_header_declares_the_path():
+    names = declared_functions()
+    for required in ("fkc_assign", "fkc_update", "fkc_update_sorted", "fkc_update_sorted_indexed",
+                     "fkc_finalize", "fkc_lloyd_iter", "fkc_lloyd_local", "fkc_lloyd_finalize",
+                     "fkc_last_error"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from flash_kmeans_cuda import _lib
+
+    raw = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in sorted(declared_functions()) if not hasattr(raw, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    assert set(_lib.EXPORTED) == declared_functions(), "ctypes signatures out of sync with header"
+
+
+def test_status_strings_and_version():
+    from flash_kmeans_cuda import _lib
+
+    assert _lib.lib.fkc_abi_version() == 1
+    assert _lib.lib.fkc_status_string(-5) == b"FKC_EWORKSPACE"
+    assert _lib.lib.fkc_status_string(0) == b"FKC_OK"
+
+
+@pytest.mark.parametrize("args,code,msg", [
+    ((0, 1, 1, 1, 0), -1, "must be >= 1"),
+    ((1, 1, 1, 1, 9), -1, "dtype"),
+    ((1, 1 << 31, 1, 1, 0), -1, "int32"),
+])
+def test_assign_rejects_bad_dims(args, code, msg):
+    from flash_kmeans_cuda import _lib
+
+    B, N, K, D, dt = args
+    st = _lib.lib.fkc_assign(1, 1, None, None, 1, B, N, K, D, dt, None, 0, None)
+    assert st == code and msg in _lib.last_error()
+
+
+def test_null_pointers_and_workspace_checks():
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    assert L.fkc_assign(None, 1, None, None, 1, 1, 8, 2, 16, 0, None, 0, None) == -1
+    assert "non-null" in _lib.last_error()
+    assert L.fkc_update(1, 1, 1, 1, 1, 10, 4, 8, 0, None, 0, None) == -5
+    need = L.fkc_lloyd_workspace_size(1, 10, 4, 16, 0)
+    assert L.fkc_lloyd_local(1, 1, 1, 1, 1, 1, 10, 4, 16, 0, 256, need - 1, None) == -5
+    assert L.fkc_lloyd_local(1, 1, 1, 1, 1, 1, 10, 4, 16, 0, 8, need, None) == -1
+    assert "256-byte aligned" in _lib.last_error()
+
+
+def test_workspace_sizes_are_device_independent():
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    # tensor-core shapes carry the norm-extension rows (32 B per point and per centroid)
+    a = L.fkc_assign_workspace_size(1, 1000, 100, 128, 0)
+    assert a >= 1000 * 32 + 100 * 32
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == 0  # fp32: CUDA-core kernel
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 100, 0) == 0  # D % 16 != 0
+    u = L.fkc_update_workspace_size(2, 1000, 100)
+    assert u >= 2 * (2 * 1000 * 4 + 2 * 100 * 4)
+    assert L.fkc_lloyd_workspace_size(1, 1000, 100, 128, 0) >= (
+        a + L.fkc_update_workspace_size(1, 1000, 100))
+
+
+def test_device_queries_without_gpu():
+    import torch
+
+    from flash_kmeans_cuda import _lib
+
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    assert _lib.lib.fkc_device_supported() == 0
+    assert _lib.lib.fkc_kernel_launches() == 0

@@ -1,0 +1,153 @@
+"""End-to-end batch_kmeans_Euclid parity on the GPU against the float64 oracle.
+
+Two kinds of checks:
+* teacher-forced: every iteration of the GPU loop is replayed by the oracle
+  from the GPU's own input centroids, so one near-tie flip cannot cascade;
+  labels must match above the gap threshold, counts exactly, centroids within
+  1e-3 relative (+ one ulp of the compute dtype);
+* free-running: both loops from the same initial centroids; final inertia
+  within 0.05% and label agreement >= 99.9% on well-separated mixtures.
+Also restates the reference's API tests (tests/test_shapes.py,
+tests/test_dtypes.py, tests/test_correctness.py:16-25 init convention).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.lloyd as orc
+from _data import TORCH_DTYPES, iid, mixture, subset_init, to_np
+
+pytestmark = pytest.mark.gpu
+
+ULP = {"float16": 2.0 ** -10, "bfloat16": 2.0 ** -7, "float32": 2.0 ** -23}
+
+
+def _close_centroids(got, ref, dtype, rel=1e-3):
+    tol = rel * np.abs(ref) + ULP[dtype] * np.abs(ref) + 1e-6
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{int(bad.sum())} centroid entries off (max {np.abs(got - ref).max()})"
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("B,N,K,D,zipf", [
+    (1, 20000, 256, 128, 0.0),
+    (1, 30000, 1024, 128, 1.1),
+    (4, 4096, 64, 64, 0.0),
+    (1, 5000, 100, 96, 0.0),
+])
+def test_teacher_forced_iterations(cuda_device, dtype, B, N, K, D, zipf):
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    x = mixture(B, N, D, K, seed=N + K, zipf=zipf, dtype=dtype)
+    c = subset_init(x, K, seed=2)
+    xd = x.cuda()
+    st = LloydState(xd, K)
+    cur = c.cuda()
+    st.set_centroids(cur)
+    xn = to_np(x)
+    for it in range(4):
+        nxt = torch.empty_like(cur)
+        st.step(cur, nxt, True)
+        torch.cuda.synchronize()
+        cn = to_np(cur)
+        ref = orc.assign(xn, cn)
+        ids = st.ids.cpu().numpy()
+        assert not ((ids != ref.ids) & ref.gap_mask()).any(), f"iter {it}: label mismatch"
+        assert (ids == ref.ids).mean() >= 0.999
+        counts = st.counts.cpu().numpy()
+        s_ref, c_ref = orc.update(xn, ids, K)
+        assert np.array_equal(counts, c_ref), f"iter {it}: counts"
+        fin = orc.finalize(s_ref, c_ref, cn, dtype)
+        _close_centroids(to_np(nxt), fin, dtype)
+        assert abs(st.shift.item() - orc.shift(to_np(nxt), cn)) <= 1e-3 * orc.shift(fin, cn) + 1e-3
+        cur = nxt
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_free_running_inertia(cuda_device, dtype):
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    B, N, K, D = 1, 32768, 256, 128
+    x = mixture(B, N, D, K, seed=11, dtype=dtype)
+    init = subset_init(x, K, seed=12)
+    ids, cents, n = batch_kmeans_Euclid(x.cuda(), K, max_iters=10, tol=0.0,
+                                        init_centroids=init.cuda())
+    torch.cuda.synchronize()
+    assert n == 10 and ids.dtype == torch.int32 and cents.dtype == TORCH_DTYPES[dtype]
+    ref = orc.lloyd(to_np(x), to_np(init), 10, 0.0, dtype)
+    xn = to_np(x)
+    inert_gpu = orc.inertia(xn, to_np(cents), ids.cpu().numpy())
+    inert_ref = orc.inertia(xn, ref.centroids, ref.ids)
+    assert abs(inert_gpu - inert_ref) <= 5e-4 * inert_ref
+    assert (ids.cpu().numpy() == ref.ids).mean() >= 0.999
+
+
+@pytest.mark.parametrize("B,N,K,D", [
+    (1, 100, 8, 64), (1, 257, 16, 128), (1, 1024, 1, 64), (1, 1024, 63, 64),
+    (1, 1024, 65, 64), (1, 1024, 32, 256), (3, 2048, 32, 64),
+])
+def test_shapes(cuda_device, B, N, K, D):
+    """tests/test_shapes.py:11-31 of the reference."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    x = torch.randn(B, N, D, device="cuda", dtype=torch.float16)
+    ids, cents, n_iters = batch_kmeans_Euclid(x, K, max_iters=3, tol=0.0)
+    assert ids.shape == (B, N) and ids.dtype == torch.int32
+    assert cents.shape == (B, K, D) and cents.dtype == torch.float16
+    assert (ids >= 0).all() and (ids < K).all()
+    assert n_iters == 3
+
+
+@pytest.mark.parametrize("K", [256, 2048, 4096, 8192])
+def test_large_k_single_iteration(cuda_device, K):
+    """tests/test_shapes.py:34-53: one iteration against the exact assignment."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    torch.manual_seed(123)
+    x = torch.randn(1, 256, 128, device="cuda", dtype=torch.float16)
+    init = torch.randn(1, K, 128, device="cuda", dtype=torch.float16)
+    ids, cents, n = batch_kmeans_Euclid(x, K, max_iters=1, tol=0.0, init_centroids=init)
+    ref = orc.assign(to_np(x), to_np(init))
+    got = ids.cpu().numpy()
+    assert n == 1 and not ((got != ref.ids) & ref.gap_mask()).any()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_kmeans_dtype(cuda_device, dtype):
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    x = torch.randn(2, 2048, 64, device="cuda", dtype=dtype)
+    ids, cents, n_iters = batch_kmeans_Euclid(x, 32, max_iters=5, tol=0.0)
+    assert cents.dtype == dtype and n_iters == 5
+
+
+def test_tol_stops_early_and_init_untouched(cuda_device, capsys):
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    x = mixture(1, 8192, 64, 16, seed=4).cuda()
+    init = subset_init(x.cpu(), 16, seed=5).cuda()
+    keep = init.clone()
+    ids, cents, n = batch_kmeans_Euclid(x, 16, max_iters=200, tol=1e-4, init_centroids=init,
+                                        verbose=True)
+    assert 1 <= n < 200
+    assert torch.equal(init, keep)
+    out = capsys.readouterr().out
+    assert out.count("center shift") == n
+    # converged: one more iteration from the result moves nothing
+    ids2, cents2, _ = batch_kmeans_Euclid(x, 16, max_iters=1, init_centroids=cents)
+    assert torch.equal(ids, ids2)
+
+
+def test_kmeans_rejects_bad_input(cuda_device):
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    with pytest.raises(AssertionError):
+        batch_kmeans_Euclid(torch.randn(1, 10, 4), 2)
+    with pytest.raises(AssertionError):
+        batch_kmeans_Euclid(torch.randn(10, 4, device="cuda"), 2)
+    with pytest.raises(RuntimeError, match="share dtype"):
+        batch_kmeans_Euclid(torch.randn(1, 10, 16, device="cuda", dtype=torch.float16), 2,
+                            init_centroids=torch.randn(1, 2, 16, device="cuda"))
