@@ -9,37 +9,44 @@
 // accumulate in fp32.
 //
 // Scoring. The MMA computes, per (row, centroid),
-//     acc = x.c - 0.5*||x||^2 - 0.5*||c||^2 = -0.5 * ||x - c||^2
-// The two norm terms enter through one extra K=16 slice of bf16 operands:
-//     A_ext[row] = {h1(x), h2(x), h3(x), 1, 1, 1, 0...}
-//     B_ext[k]   = {1, 1, 1, h1(c), h2(c), h3(c), 0...}
+//     acc = x.c - 0.5*||x||^2 - 0.5*||c||^2 - delta = -0.5 * ||x - c||^2 - delta
+// The norm terms enter through one extra K=16 slice of bf16 operands:
+//     A_ext[row] = {h1(x), h2(x), h3(x), 1, 1, 1, -delta(x), 0...}
+//     B_ext[k]   = {1, 1, 1, h1(c), h2(c), h3(c), 1, 0...}
 // where h1+h2+h3 is a three-term bf16 split (24 significant bits) of
-// -0.5*||.||^2. So TMEM holds -dist/2 directly and the epilogue needs no
-// per-column c_sq load and no FMA.
+// -0.5*||.||^2 and delta = 2^-12 ||x||^2 (+ 2^-100) is a row-constant bias.
+// So TMEM holds -dist/2 - delta directly: no per-column c_sq load and no FMA
+// in the epilogue, and the score is strictly negative whenever c_sq is the
+// centroids' own norm (rounding of the fp32 accumulation is ~2^-22 ||x||^2).
 //
-// Argmin on packed keys. -dist/2 <= 0 up to rounding, and the IEEE bit
-// pattern of a non-positive float, read as an unsigned integer, grows with
-// the distance; tiny positive values (computed distance < 0 from rounding)
-// sort before all negative ones, i.e. as "distance ~ 0". The epilogue replaces
-// the 5 low mantissa bits with the column index j inside a 32-column group and
-// takes an unsigned min: 2 instructions per score (LOP3 + IMNMX). Exact ties
-// within a group resolve to the lowest j; groups and chunks are merged in
-// ascending k with a strict comparison of the truncated keys, so exact ties
-// across groups resolve to the lowest k as well. The truncation only affects
-// candidates within 2^-18 relative distance of each other.
+// Argmax on packed keys. The epilogue replaces the 5 low mantissa bits of each
+// score with its column index j inside a 32-column group (one LOP3) and takes
+// a float max with 3-input max.f32 (about half an instruction per score). For
+// negative scores a larger j makes the key more negative, so exact ties within
+// a group resolve to the lowest j; groups and chunks are merged in ascending k
+// with a strict comparison of the truncated keys, so exact ties across groups
+// resolve to the lowest k as well (the reference's rule). The truncation only
+// affects candidates within 2^-18 relative score of each other. Scores of any
+// sign order correctly (a caller's c_sq may make them positive); only exact
+// ties between positive scores would go to the higher j.
 //
-// Kernel structure (one persistent CTA per SM, 192 threads):
+// Kernel structure (one persistent CTA per SM, 320 threads):
 //   warp 0      TMA producer: x sub-tiles (+ row-norm slice) once per tile,
 //               centroid chunks (+ norm slice) through an ST-deep ring.
 //   warp 1      TMEM owner and MMA issuer (one thread): for each (chunk,
 //               sub-tile) item, D/16 fp16/bf16 MMAs + 1 bf16 norm MMA into
 //               one of two TMEM accumulator slots.
-//   warps 2..5  epilogue: one TMEM lane (= one x row) per thread; tcgen05.ld
-//               32 columns at a time, packed-key min, running best per row.
+//   warps 2..9  epilogue, two warpgroups of four: one TMEM lane (= one x row)
+//               per thread, the first / second half of each item's columns;
+//               tcgen05.ld 32 columns at a time, packed-key max, running best
+//               per row; the halves merge once per tile.
 // Two accumulator slots ping-pong so the epilogue of one item overlaps the
-// MMAs of the next.
+// MMAs of the next; two warps per scheduler hide the ALU latencies.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <cmath>
+#include <utility>
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
@@ -54,7 +61,7 @@ constexpr int kRowsPerSub = 128;  // UMMA M (one TMEM lane per row)
 constexpr int kKBlockElems = 64;  // elements of one 128-byte swizzle row (16-bit types)
 constexpr int kKBlockBytes = 128;
 constexpr int kExtBytes = 32;     // 16 bf16 of the norm slice
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kEpiWarpBegin = 2;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
 
@@ -71,9 +78,11 @@ struct Cfg {
   static constexpr int kOffCext = kOffAext + MT * kAextSubBytes;
   static constexpr int kOffBar = kOffCext + ST * kCextStageBytes;
   // x_full[MT] x_empty[MT] c_full[ST] c_empty[ST] acc_full[2] acc_empty[2] drain
-  static constexpr int kNumBars = 2 * MT + 2 * ST + 5;
+  // merge_full merge_empty
+  static constexpr int kNumBars = 2 * MT + 2 * ST + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1 KB alignment
+  static constexpr int kOffMerge = kOffMisc + 16;  // half-1 best per row: MT*128 x (f32, i32)
+  static constexpr int kSmemBytes = kOffMerge + MT * kRowsPerSub * 8 + 1024;  // + align slack
   static constexpr uint32_t kXTxBytes = kXSubBytes + kAextSubBytes;
   static constexpr uint32_t kCTxBytes = kCStageBytes + kCextStageBytes;
   static constexpr uint32_t kTmemCols = 2 * NC;
@@ -97,6 +106,12 @@ struct Cfg {
   }
   __device__ static uint32_t drain(uint32_t base) {
     return base + kOffBar + 8 * (2 * MT + 2 * ST + 4);
+  }
+  __device__ static uint32_t merge_full(uint32_t base) {
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + 5);
+  }
+  __device__ static uint32_t merge_empty(uint32_t base) {
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + 6);
   }
 };
 
@@ -129,39 +144,74 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
       : "memory");
 }
 
-// Min over 32 packed keys (score bits with j in the 5 low bits).
+// Packed key of column j: the score's bits with the 5 low mantissa bits
+// replaced by j, (bits & ~31) | j, one LOP3 with j as an immediate.
+template <int J>
+__device__ __forceinline__ float pack_key(uint32_t bits, uint32_t mask) {
+  uint32_t k;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEC;" : "=r"(k) : "r"(bits), "n"(J), "r"(mask));
+  return __uint_as_float(k);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ float fmax2(float a, float b) {
+  float d;
+  asm("max.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+template <int... J>
+__device__ __forceinline__ void pack_group(const uint32_t (&r)[32], float (&v)[32],
+                                           uint32_t mask, std::integer_sequence<int, J...>) {
+  ((v[J] = pack_key<J>(r[J], mask)), ...);
+}
+
+// Max over 32 packed keys with 3-input max (17 ops). Scores are negative
+// (-dist/2 - delta), so among keys of equal truncated score the one with the
+// lowest j is the largest: ties resolve to the lowest column.
 template <bool MASKED>
-__device__ __forceinline__ uint32_t group_min(const uint32_t (&r)[32], int nvalid) {
-  uint32_t k[32];
+__device__ __forceinline__ float group_max(const uint32_t (&r)[32], uint32_t mask, int nvalid) {
+  float v[32];
+  pack_group(r, v, mask, std::make_integer_sequence<int, 32>{});
+  if (MASKED) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    uint32_t key = (r[j] & 0xFFFFFFE0u) | static_cast<uint32_t>(j);
-    if (MASKED) key = (j < nvalid) ? key : 0xFFFFFFFFu;
-    k[j] = key;
+    for (int j = 0; j < 32; ++j) v[j] = (j < nvalid) ? v[j] : -INFINITY;
   }
+  float m1[11];
 #pragma unroll
-  for (int w = 16; w >= 1; w >>= 1) {
+  for (int i = 0; i < 10; ++i) m1[i] = fmax3(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  m1[10] = fmax2(v[30], v[31]);
+  float m2[4];
 #pragma unroll
-    for (int j = 0; j < w; ++j) k[j] = min(k[j], k[j + w]);
-  }
-  return k[0];
+  for (int i = 0; i < 3; ++i) m2[i] = fmax3(m1[3 * i], m1[3 * i + 1], m1[3 * i + 2]);
+  m2[3] = fmax2(m1[9], m1[10]);
+  return fmax2(fmax3(m2[0], m2[1], m2[2]), m2[3]);
 }
 
-__device__ __forceinline__ void merge_best(uint32_t m, int col0, uint32_t& best_trunc,
-                                           int& best_idx) {
-  const uint32_t mt = m & 0xFFFFFFE0u;
-  if (mt < best_trunc) {
-    best_trunc = mt;
-    best_idx = col0 + static_cast<int>(m & 31u);
+// Folds a group's winner into the running best. Groups arrive in ascending
+// column order and only a strictly larger truncated score replaces the best,
+// so exact ties keep the lowest column.
+__device__ __forceinline__ void merge_best(float m, int col0, float& best_val, int& best_idx) {
+  const uint32_t mb = __float_as_uint(m);
+  const float mt = __uint_as_float(mb & 0xFFFFFFE0u);
+  if (mt > best_val) {
+    best_val = mt;
+    best_idx = col0 + static_cast<int>(mb & 31u);
   }
 }
 
-// Reads NC accumulator columns of this thread's TMEM lane and folds them into
+// Reads NCH accumulator columns of this thread's TMEM lane and folds them into
 // the running best. Loads of group g+1 are in flight while group g is reduced.
-template <int NC, bool MASKED>
-__device__ __forceinline__ void epilogue_item(uint32_t taddr, int valid, int cbase,
-                                              uint32_t& best_trunc, int& best_idx) {
-  constexpr int G = NC / 32;
+template <int NCH, bool MASKED>
+__device__ __forceinline__ void epilogue_item(uint32_t taddr, int valid, int col0,
+                                              float& best_val, int& best_idx) {
+  constexpr int G = NCH / 32;
+  const uint32_t mask = 0xFFFFFFE0u;
   uint32_t ra[32], rb[32];
   tmem_ld_32x32b_x32(taddr, ra);
   tmem_wait_ld_regs(ra);
@@ -169,11 +219,11 @@ __device__ __forceinline__ void epilogue_item(uint32_t taddr, int valid, int cba
   for (int g = 0; g < G; ++g) {
     if ((g & 1) == 0) {
       if (g + 1 < G) tmem_ld_32x32b_x32(taddr + (g + 1) * 32, rb);
-      merge_best(group_min<MASKED>(ra, valid - g * 32), cbase + g * 32, best_trunc, best_idx);
+      merge_best(group_max<MASKED>(ra, mask, valid - g * 32), col0 + g * 32, best_val, best_idx);
       if (g + 1 < G) tmem_wait_ld_regs(rb);
     } else {
       if (g + 1 < G) tmem_ld_32x32b_x32(taddr + (g + 1) * 32, ra);
-      merge_best(group_min<MASKED>(rb, valid - g * 32), cbase + g * 32, best_trunc, best_idx);
+      merge_best(group_max<MASKED>(rb, mask, valid - g * 32), col0 + g * 32, best_val, best_idx);
       if (g + 1 < G) tmem_wait_ld_regs(ra);
     }
   }
@@ -209,9 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(C::acc_full(sb, a), 1);
-      mbar_init(C::acc_empty(sb, a), 4);  // one arrival per epilogue warp
+      mbar_init(C::acc_empty(sb, a), 8);  // one arrival per epilogue warp
     }
     mbar_init(C::drain(sb), 1);
+    mbar_init(C::merge_full(sb), 4);   // the four half-1 warps
+    mbar_init(C::merge_empty(sb), 4);  // the four half-0 warps
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -358,24 +410,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
+    // Two warpgroups: half 0 reads the first NC/2 columns of every item, half 1
+    // the last NC/2, each for all 128 TMEM lanes (one x row per thread). At the
+    // end of a tile half 1 hands its per-row best to half 0 through shared
+    // memory (bounded mbarrier handshake) and half 0 writes the labels.
+    constexpr int NCH = NC / 2;
+    const int epi = warp - kEpiWarpBegin;  // 0..7
+    const int half = epi >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_sub = q * 32 + lane;
-    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    uint32_t item = 0;
+    const uint32_t lane_addr =
+        tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * NCH);
+    float* merge_val = reinterpret_cast<float*>(smem + C::kOffMerge);
+    int* merge_idx = reinterpret_cast<int*>(smem + C::kOffMerge + MT * kRowsPerSub * 4);
+    uint32_t item = 0, tcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
       const int b = tile / tiles_per_batch;
       const int row0 = (tile - b * tiles_per_batch) * (MT * kRowsPerSub);
-      uint32_t best_trunc[MT];
+      float best_val[MT];
       int best_idx[MT];
 #pragma unroll
       for (int s = 0; s < MT; ++s) {
-        best_trunc[s] = 0xFFFFFFE0u;
+        best_val[s] = -INFINITY;
         best_idx[s] = 0;
       }
       for (int ch = 0; ok && ch < nchunks; ++ch) {
-        const int cbase = ch * NC;
-        const int valid = min(NC, K - cbase);
+        const int col0 = ch * NC + half * NCH;
+        const int valid = min(NCH, K - col0);  // may be <= 0 for half 1 of the last chunk
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
           const uint32_t slot = item & 1u;
@@ -389,10 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t taddr = lane_addr + slot * NC;
-          if (valid == NC)
-            epilogue_item<NC, false>(taddr, valid, cbase, best_trunc[s], best_idx[s]);
-          else
-            epilogue_item<NC, true>(taddr, valid, cbase, best_trunc[s], best_idx[s]);
+          if (valid >= NCH)
+            epilogue_item<NCH, false>(taddr, valid, col0, best_val[s], best_idx[s]);
+          else if (valid > 0)
+            epilogue_item<NCH, true>(taddr, valid, col0, best_val[s], best_idx[s]);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(C::acc_empty(sb, slot));
@@ -400,6 +462,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
+      const uint32_t mph = tcount & 1u;
+      if (half == 1) {
+        int got = 1;
+        if (lane == 0) got = mbar_wait(C::merge_empty(sb), mph ^ 1u, abort_flag);
+        got = __shfl_sync(0xFFFFFFFFu, got, 0);
+        if (!got) {
+          if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
+          break;
+        }
+#pragma unroll
+        for (int s = 0; s < MT; ++s) {
+          merge_val[s * kRowsPerSub + row_in_sub] = best_val[s];
+          merge_idx[s * kRowsPerSub + row_in_sub] = best_idx[s];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(C::merge_full(sb));
+        continue;
+      }
+      int got = 1;
+      if (lane == 0) got = mbar_wait(C::merge_full(sb), mph, abort_flag);
+      got = __shfl_sync(0xFFFFFFFFu, got, 0);
+      if (!got) {
+        if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
+        break;
+      }
+#pragma unroll
+      for (int s = 0; s < MT; ++s) {
+        const float v1 = merge_val[s * kRowsPerSub + row_in_sub];
+        const int i1 = merge_idx[s * kRowsPerSub + row_in_sub];
+        if (v1 > best_val[s] || (v1 == best_val[s] && i1 < best_idx[s])) best_idx[s] = i1;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(C::merge_empty(sb));
 #pragma unroll
       for (int s = 0; s < MT; ++s) {
         const int row = row0 + s * kRowsPerSub + row_in_sub;

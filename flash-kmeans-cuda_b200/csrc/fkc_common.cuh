@@ -53,18 +53,23 @@ __device__ __forceinline__ void split3_bf16(float v, uint32_t& h1, uint32_t& h2,
   h3 = __bfloat16_as_ushort(b3);
 }
 
-// Row side (x):        {h1, h2, h3, 1, 1, 1, 0 x 10}
-// Centroid side (c):   {1, 1, 1, h1, h2, h3, 0 x 10}
-// so that <row_ext, centroid_ext> = value(row) + value(centroid).
+// Row side (x):        {h1, h2, h3, 1, 1, 1, -delta, 0 x 9}
+// Centroid side (c):   {1, 1, 1, h1, h2, h3, 1,      0 x 9}
+// so that <row_ext, centroid_ext> = value(row) + value(centroid) - delta(row),
+// with value = -||.||^2 / 2 and delta = 2^-12 ||x||^2 + 2^-100 a row-constant
+// bias (it does not change a row's argmin) that keeps every score -dist/2 -
+// delta strictly negative, far above the fp32 rounding of the accumulation.
 __device__ __forceinline__ void write_norm_ext(void* dst, float value, bool row_side) {
   uint32_t h1, h2, h3;
   split3_bf16(value, h1, h2, h3);
   const uint32_t one = 0x3F80u;  // bf16 1.0
   uint4 lo;
   if (row_side) {
-    lo = make_uint4(h1 | (h2 << 16), h3 | (one << 16), one | (one << 16), 0u);
+    const float delta = fmaf(-value, 0x1p-11f, 0x1p-100f);
+    const uint32_t nd = __bfloat16_as_ushort(__float2bfloat16_rn(-delta));
+    lo = make_uint4(h1 | (h2 << 16), h3 | (one << 16), one | (one << 16), nd);
   } else {
-    lo = make_uint4(one | (one << 16), one | (h1 << 16), h2 | (h3 << 16), 0u);
+    lo = make_uint4(one | (one << 16), one | (h1 << 16), h2 | (h3 << 16), one);
   }
   uint4* d = reinterpret_cast<uint4*>(dst);
   d[0] = lo;
