@@ -21,7 +21,7 @@
 //
 // Argmax on packed keys. The epilogue replaces the 5 low mantissa bits of each
 // score with its column index j inside a 32-column group (one LOP3) and takes
-// a float max with 3-input max.f32 (about half an instruction per score). For
+// a float max with 3-input max.f32 (about half an issue slot per score). For
 // negative scores a larger j makes the key more negative, so exact ties within
 // a group resolve to the lowest j; groups and chunks are merged in ascending k
 // with a strict comparison of the truncated keys, so exact ties across groups
@@ -30,16 +30,16 @@
 // sign order correctly (a caller's c_sq may make them positive); only exact
 // ties between positive scores would go to the higher j.
 //
-// Kernel structure (one persistent CTA per SM, 320 threads):
+// Kernel structure (one persistent CTA per SM, 64 + 32*kEpiWarps threads):
 //   warp 0      TMA producer: x sub-tiles (+ row-norm slice) once per tile,
 //               centroid chunks (+ norm slice) through an ST-deep ring.
 //   warp 1      TMEM owner and MMA issuer (one thread): for each (chunk,
 //               sub-tile) item, D/16 fp16/bf16 MMAs + 1 bf16 norm MMA into
 //               one of two TMEM accumulator slots.
-//   warps 2..9  epilogue, two warpgroups of four: one TMEM lane (= one x row)
-//               per thread, the first / second half of each item's columns;
+//   warps 2..   epilogue, kEpiWarps/4 warpgroups: one TMEM lane (= one x row)
+//               per thread, one column slice of each item per warpgroup;
 //               tcgen05.ld 32 columns at a time, packed-key max, running best
-//               per row; the halves merge once per tile.
+//               per row; the slices merge once per tile.
 // Two accumulator slots ping-pong so the epilogue of one item overlaps the
 // MMAs of the next; two warps per scheduler hide the ALU latencies.
 #include <cuda_bf16.h>
@@ -61,7 +61,11 @@ constexpr int kRowsPerSub = 128;  // UMMA M (one TMEM lane per row)
 constexpr int kKBlockElems = 64;  // elements of one 128-byte swizzle row (16-bit types)
 constexpr int kKBlockBytes = 128;
 constexpr int kExtBytes = 32;     // 16 bf16 of the norm slice
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+// Epilogue warps: two per TMEM lane quarter (= per SM sub-partition). Measured
+// on B200 at c3 (assign ms): 8 warps 0.894, 16 warps 0.950 (more issue
+// overhead per score); without any epilogue the MMA/TMA pipeline takes 0.784.
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilogue
 constexpr int kEpiWarpBegin = 2;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
 
@@ -81,8 +85,9 @@ struct Cfg {
   // merge_full merge_empty
   static constexpr int kNumBars = 2 * MT + 2 * ST + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kOffMerge = kOffMisc + 16;  // half-1 best per row: MT*128 x (f32, i32)
-  static constexpr int kSmemBytes = kOffMerge + MT * kRowsPerSub * 8 + 1024;  // + align slack
+  // best per row of column parts 1..3: 3 x MT*128 x (f32, i32)
+  static constexpr int kOffMerge = kOffMisc + 16;
+  static constexpr int kSmemBytes = kOffMerge + 3 * MT * kRowsPerSub * 8 + 1024;  // + align slack
   static constexpr uint32_t kXTxBytes = kXSubBytes + kAextSubBytes;
   static constexpr uint32_t kCTxBytes = kCStageBytes + kCextStageBytes;
   static constexpr uint32_t kTmemCols = 2 * NC;
@@ -171,9 +176,11 @@ __device__ __forceinline__ void pack_group(const uint32_t (&r)[32], float (&v)[3
   ((v[J] = pack_key<J>(r[J], mask)), ...);
 }
 
-// Max over 32 packed keys with 3-input max (17 ops). Scores are negative
-// (-dist/2 - delta), so among keys of equal truncated score the one with the
-// lowest j is the largest: ties resolve to the lowest column.
+// Max over 32 packed keys: 15 three-input + 2 two-input max.f32 (17 issue
+// slots; measured on B200, 3-input max runs at half the 2-input rate, so the
+// win is issue slots, not ALU cycles). Scores are negative (-dist/2 - delta),
+// so among keys of equal truncated score the one with the lowest j is the
+// largest: ties resolve to the lowest column.
 template <bool MASKED>
 __device__ __forceinline__ float group_max(const uint32_t (&r)[32], uint32_t mask, int nvalid) {
   float v[32];
@@ -193,16 +200,19 @@ __device__ __forceinline__ float group_max(const uint32_t (&r)[32], uint32_t mas
   return fmax2(fmax3(m2[0], m2[1], m2[2]), m2[3]);
 }
 
-// Folds a group's winner into the running best. Groups arrive in ascending
-// column order and only a strictly larger truncated score replaces the best,
-// so exact ties keep the lowest column.
+// Folds a group's winner into the running best (predicated, no branch).
+// Groups arrive in ascending column order and only a strictly larger
+// truncated score replaces the best, so exact ties keep the lowest column.
 __device__ __forceinline__ void merge_best(float m, int col0, float& best_val, int& best_idx) {
   const uint32_t mb = __float_as_uint(m);
   const float mt = __uint_as_float(mb & 0xFFFFFFE0u);
-  if (mt > best_val) {
-    best_val = mt;
-    best_idx = col0 + static_cast<int>(mb & 31u);
-  }
+  const int cand = col0 + static_cast<int>(mb & 31u);
+  asm("{\n\t.reg .pred p;\n\t"
+      "setp.gt.f32 p, %2, %0;\n\t"
+      "selp.f32 %0, %2, %0, p;\n\t"
+      "selp.b32 %1, %3, %1, p;\n\t}"
+      : "+f"(best_val), "+r"(best_idx)
+      : "f"(mt), "r"(cand));
 }
 
 // Reads NCH accumulator columns of this thread's TMEM lane and folds them into
@@ -259,11 +269,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(C::acc_full(sb, a), 1);
-      mbar_init(C::acc_empty(sb, a), 8);  // one arrival per epilogue warp
+      mbar_init(C::acc_empty(sb, a), kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(C::drain(sb), 1);
-    mbar_init(C::merge_full(sb), 4);   // the four half-1 warps
-    mbar_init(C::merge_empty(sb), 4);  // the four half-0 warps
+    mbar_init(C::merge_full(sb), kEpiWarps - 4);  // the warps of column parts 1..3
+    mbar_init(C::merge_empty(sb), 4);             // the four warps of part 0
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -410,19 +420,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    // Two warpgroups: half 0 reads the first NC/2 columns of every item, half 1
-    // the last NC/2, each for all 128 TMEM lanes (one x row per thread). At the
-    // end of a tile half 1 hands its per-row best to half 0 through shared
-    // memory (bounded mbarrier handshake) and half 0 writes the labels.
-    constexpr int NCH = NC / 2;
-    const int epi = warp - kEpiWarpBegin;  // 0..7
-    const int half = epi >> 2;
+    // kParts warpgroups: part p reads columns [p*NCP, (p+1)*NCP) of every item
+    // for all 128 TMEM lanes (one x row per thread). At the end of a tile parts
+    // 1.. hand their per-row best to part 0 through shared memory (bounded
+    // mbarrier handshake) and part 0 writes the labels.
+    constexpr int kParts = kEpiWarps / 4;
+    constexpr int NCH = NC / kParts;
+    static_assert(NCH % 32 == 0, "each epilogue part reads whole 32-column groups");
+    const int epi = warp - kEpiWarpBegin;
+    const int part = epi >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_sub = q * 32 + lane;
     const uint32_t lane_addr =
-        tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half * NCH);
+        tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(part * NCH);
     float* merge_val = reinterpret_cast<float*>(smem + C::kOffMerge);
-    int* merge_idx = reinterpret_cast<int*>(smem + C::kOffMerge + MT * kRowsPerSub * 4);
+    int* merge_idx =
+        reinterpret_cast<int*>(smem + C::kOffMerge + (kParts - 1) * MT * kRowsPerSub * 4);
     uint32_t item = 0, tcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
@@ -436,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         best_idx[s] = 0;
       }
       for (int ch = 0; ok && ch < nchunks; ++ch) {
-        const int col0 = ch * NC + half * NCH;
-        const int valid = min(NCH, K - col0);  // may be <= 0 for half 1 of the last chunk
+        const int col0 = ch * NC + part * NCH;
+        const int valid = min(NCH, K - col0);  // may be <= 0 in the last chunk
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
           const uint32_t slot = item & 1u;
@@ -463,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       const uint32_t mph = tcount & 1u;
-      if (half == 1) {
+      if (part > 0) {
         int got = 1;
         if (lane == 0) got = mbar_wait(C::merge_empty(sb), mph ^ 1u, abort_flag);
         got = __shfl_sync(0xFFFFFFFFu, got, 0);
@@ -473,8 +486,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
-          merge_val[s * kRowsPerSub + row_in_sub] = best_val[s];
-          merge_idx[s * kRowsPerSub + row_in_sub] = best_idx[s];
+          const int slot_m = ((part - 1) * MT + s) * kRowsPerSub + row_in_sub;
+          merge_val[slot_m] = best_val[s];
+          merge_idx[slot_m] = best_idx[s];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(C::merge_full(sb));
@@ -489,9 +503,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int s = 0; s < MT; ++s) {
-        const float v1 = merge_val[s * kRowsPerSub + row_in_sub];
-        const int i1 = merge_idx[s * kRowsPerSub + row_in_sub];
-        if (v1 > best_val[s] || (v1 == best_val[s] && i1 < best_idx[s])) best_idx[s] = i1;
+#pragma unroll
+        for (int p = 1; p < kParts; ++p) {
+          const int slot_m = ((p - 1) * MT + s) * kRowsPerSub + row_in_sub;
+          const float v1 = merge_val[slot_m];
+          const int i1 = merge_idx[slot_m];
+          if (v1 > best_val[s] || (v1 == best_val[s] && i1 < best_idx[s])) {
+            best_val[s] = v1;
+            best_idx[s] = i1;
+          }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(C::merge_empty(sb));

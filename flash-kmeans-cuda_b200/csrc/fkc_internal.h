@@ -11,7 +11,7 @@
 #include <cstdio>
 #include <string>
 
-#include "../../include/fkc_capi.h"
+#include "fkc_capi.h"  // include/ is on the include path
 
 namespace fkc {
 
