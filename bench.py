@@ -213,10 +213,81 @@ def cpu_baseline(w: dict, workload: str) -> dict:
                        f"oracle/cpu_lloyd.py), median of 3, scaled by {scale:.1f}x")}
 
 
+def run_reference_gpu(args, w: dict) -> None:
+    """The reference's own CUDA kernels (oracle/_ref, built from its sources) on the
+    same workload, one GPU: a step is one Lloyd iteration of the reference's loop
+    (c_sq, fkc::euclid_assign, torch.sort + sorted/indexed accumulate, finalize)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import ref_lloyd
+
+    if not ref_lloyd.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "oracle/_ref not built (oracle/build_ref.sh needs the reference sources)"}))
+        return
+    ref = ref_lloyd.Reference()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    x, init = make_data(w, dev, seed=0)
+    K = w["K"]
+    x_sq = (x.float() ** 2).sum(-1).contiguous()
+    cur = [init.clone()]
+
+    def step():
+        c = cur[0]
+        c_sq = (c.float() ** 2).sum(dim=-1).contiguous()
+        ids = ref.assign(x, c, x_sq=x_sq, c_sq=c_sq)
+        sums, counts = ref.update(x, ids, K)
+        cur[0] = ref.finalize(sums, counts, c)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    c = cur[0]
+    c_sq = (c.float() ** 2).sum(dim=-1).contiguous()
+    reps = 5
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ref.assign(x, c, x_sq=x_sq, c_sq=c_sq)
+    a0.record()
+    for _ in range(reps):
+        ref.assign(x, c, x_sq=x_sq, c_sq=c_sq)
+    a1.record()
+    torch.cuda.synchronize()
+    t_assign = a0.elapsed_time(a1) / reps
+    flops = 2.0 * w["B"] * w["N"] * K * w["D"]
+    peaks = measured_peaks()
+    tf = flops / (t_assign * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "K-Means ms/iter", "value": ms, "unit": "ms/iter", "impl": "reference",
+        "device": "cuda", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+        "dtype": DT_SHORT[w["dtype"]], "data": "synthetic",
+        "config": {"workload": args.workload, "B": w["B"], "N": w["N"], "K": K, "D": w["D"],
+                   "parallelism": "dp1"},
+        "assign_ms": t_assign, "assign_tflops": tf,
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["tflops"],
+                     "unit": "TFLOP/s", "frac": tf / peaks["tflops"],
+                     "kernel": "reference assign_sm80_kernel (mma.sync, fp16 accumulation)"},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_reference_arm(args, w: dict) -> None:
     """CPU port of the reference loop timed on the host cores (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.ref_device == "cuda":
+        run_reference_gpu(args, w)
         return
     from oracle.cpu_lloyd import lloyd_cpu
 
@@ -438,6 +509,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
+                    help="reference arm: the CPU port of its loop (default) or its own CUDA "
+                         "kernels built from source under oracle/_ref")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warmup raised to 3 (minimum)")
