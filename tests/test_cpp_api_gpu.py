@@ -30,7 +30,8 @@ def test_cpp_api_smoke(tmp_path, cuda_device):
            *[f"-I{p}" for p in cpp_extension.include_paths()], "-I/usr/local/cuda/include",
            f"-I{os.path.join(ROOT, 'include')}", os.path.join(ROOT, "tests", "cpp", "api_smoke.cpp"),
            "-o", exe, f"-L{LIBDIR}", "-lflash_kmeans_cuda", "-lfkc_b200", f"-L{tlib}", "-lc10",
-           "-ltorch_cpu", "-ltorch_cuda", "-lc10_cuda", f"-Wl,-rpath,{LIBDIR}", f"-Wl,-rpath,{tlib}"]
+           "-ltorch_cpu", "-ltorch_cuda", "-lc10_cuda", "-L/usr/local/cuda/lib64", "-lcudart",
+           f"-Wl,-rpath,{LIBDIR}", f"-Wl,-rpath,{tlib}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-3000:]
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
