@@ -28,7 +28,8 @@ OUT_DIR = PKG_ROOT / "flash_kmeans_cuda"
 BUILD_DIR = PKG_ROOT / "_build"
 INCLUDE = REPO_ROOT / "include"
 
-CORE_SOURCES = ["capi.cu", "assign_tc.cu", "assign_simt.cu", "update.cu", "finalize.cu"]
+CORE_SOURCES = ["capi.cu", "assign_tc.cu", "norm_ext.cu", "assign_simt.cu", "update.cu",
+                "finalize.cu"]
 CORE_LIB = OUT_DIR / "libfkc_b200.so"
 TORCH_API_LIB = OUT_DIR / "libflash_kmeans_cuda.so"
 

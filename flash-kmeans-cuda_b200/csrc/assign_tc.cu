@@ -14,10 +14,10 @@
 //     A_ext[row] = {h1(x), h2(x), h3(x), 1, 1, 1, -delta(x), 0...}
 //     B_ext[k]   = {1, 1, 1, h1(c), h2(c), h3(c), 1, 0...}
 // where h1+h2+h3 is a three-term bf16 split (24 significant bits) of
-// -0.5*||.||^2 and delta = 2^-12 ||x||^2 (+ 2^-100) is a row-constant bias.
-// So TMEM holds -dist/2 - delta directly: no per-column c_sq load and no FMA
-// in the epilogue, and the score is strictly negative whenever c_sq is the
-// centroids' own norm (rounding of the fp32 accumulation is ~2^-22 ||x||^2).
+// -0.5*||.||^2 and delta = 2^-12 ||x||^2 (+ 2^-100) is a row-constant bias
+// (norm_ext.cu). So TMEM holds -dist/2 - delta directly: no per-column c_sq
+// load and no FMA in the epilogue, and the score is strictly negative whenever
+// c_sq is the centroids' own norm (the fp32 accumulation rounds at ~2^-22 ||x||^2).
 //
 // Argmax on packed keys. The epilogue replaces the 5 low mantissa bits of each
 // score with its column index j inside a 32-column group (one LOP3) and takes
@@ -30,7 +30,7 @@
 // sign order correctly (a caller's c_sq may make them positive); only exact
 // ties between positive scores would go to the higher j.
 //
-// Kernel structure (one persistent CTA per SM, 64 + 32*kEpiWarps threads):
+// Kernel structure (persistent, one CTA per SM, 64 + 32*kEpiWarps threads):
 //   warp 0      TMA producer: x sub-tiles (+ row-norm slice) once per tile,
 //               centroid chunks (+ norm slice) through an ST-deep ring.
 //   warp 1      TMEM owner and MMA issuer (one thread): for each (chunk,
@@ -41,11 +41,26 @@
 //               tcgen05.ld 32 columns at a time, packed-key max, running best
 //               per row; the slices merge once per tile.
 // Two accumulator slots ping-pong so the epilogue of one item overlaps the
-// MMAs of the next; two warps per scheduler hide the ALU latencies.
+// MMAs of the next.
+//
+// CTA pairs (CG = 2). Launched as clusters of two CTAs on one TPC: each CTA
+// owns MT x 128 rows of a tile and loads HALF of every 256-centroid chunk; the
+// even CTA issues tcgen05.mma.cta_group::2 with M = 256 (128 rows from each
+// CTA's shared memory) and N = 256 (128 centroids from each), and every CTA's
+// TMEM receives its own 128 rows x 256 columns. Per SM this halves the shared-
+// memory operand traffic of the MMA and the L2 reads of centroid chunks, which
+// bound the single-CTA kernel (CG = 1). TMA completions of both CTAs land on
+// the even CTA's full barriers; MMA completions are fanned out to both CTAs'
+// barriers by one commit with a CTA mask; the odd CTA's epilogue releases
+// accumulator slots with a remote arrive on the even CTA's barrier. Opt-in
+// (FKC_ASSIGN_CTA_GROUP=2): single CTAs are faster here (cta_group_choice).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
 #include <utility>
 
 #include "fkc_common.cuh"
@@ -57,25 +72,28 @@ namespace {
 
 using namespace fkc::ptx;
 
-constexpr int kRowsPerSub = 128;  // UMMA M (one TMEM lane per row)
+constexpr int kRowsPerSub = 128;  // UMMA M per CTA (one TMEM lane per row)
 constexpr int kKBlockElems = 64;  // elements of one 128-byte swizzle row (16-bit types)
 constexpr int kKBlockBytes = 128;
-constexpr int kExtBytes = 32;     // 16 bf16 of the norm slice
+constexpr int kExtBytes = kNormExtBytes;  // 16 bf16 of the norm slice
 // Epilogue warps: two per TMEM lane quarter (= per SM sub-partition). Measured
-// on B200 at c3 (assign ms): 8 warps 0.894, 16 warps 0.950 (more issue
-// overhead per score); without any epilogue the MMA/TMA pipeline takes 0.784.
+// on B200 at c3 (assign ms, single CTA): 8 warps 0.894, 16 warps 0.950 (more
+// issue overhead per score); without any epilogue the single-CTA MMA/TMA
+// pipeline takes 0.784.
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilogue
 constexpr int kEpiWarpBegin = 2;
-constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block on sm_100
+constexpr int kParts = kEpiWarps / 4;          // column slices of an item
+constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
 
-template <int DB, int MT, int NC, int ST>
+template <int DB, int MT, int NC, int ST, int CG>
 struct Cfg {
+  static constexpr int kNB = NC / CG;  // centroid rows of a chunk held by one CTA
   static constexpr int kXSubBytes = DB * kRowsPerSub * kKBlockBytes;
-  static constexpr int kCBlockBytes = NC * kKBlockBytes;
+  static constexpr int kCBlockBytes = kNB * kKBlockBytes;
   static constexpr int kCStageBytes = DB * kCBlockBytes;
   static constexpr int kAextSubBytes = kRowsPerSub * kExtBytes;
-  static constexpr int kCextStageBytes = NC * kExtBytes;
+  static constexpr int kCextStageBytes = kNB * kExtBytes;
   static constexpr int kOffX = 0;
   static constexpr int kOffC = kOffX + MT * kXSubBytes;
   static constexpr int kOffAext = kOffC + ST * kCStageBytes;
@@ -85,15 +103,19 @@ struct Cfg {
   // merge_full merge_empty
   static constexpr int kNumBars = 2 * MT + 2 * ST + 7;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  // best per row of column parts 1..3: 3 x MT*128 x (f32, i32)
+  // best per row of column slices 1..kParts-1: (kParts-1) x MT*128 x (f32, i32)
   static constexpr int kOffMerge = kOffMisc + 16;
-  static constexpr int kSmemBytes = kOffMerge + 3 * MT * kRowsPerSub * 8 + 1024;  // + align slack
-  static constexpr uint32_t kXTxBytes = kXSubBytes + kAextSubBytes;
-  static constexpr uint32_t kCTxBytes = kCStageBytes + kCextStageBytes;
+  static constexpr int kSmemBytes =
+      kOffMerge + (kParts - 1) * MT * kRowsPerSub * 8 + 1024;  // + alignment slack
+  // bytes landing on a full barrier per phase (both CTAs for CG = 2)
+  static constexpr uint32_t kXTxBytes = CG * (kXSubBytes + kAextSubBytes);
+  static constexpr uint32_t kCTxBytes = CG * (kCStageBytes + kCextStageBytes);
   static constexpr uint32_t kTmemCols = 2 * NC;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget exceeded");
   static_assert(NC % 32 == 0 && NC >= 32 && NC <= 256, "UMMA N");
+  static_assert(kNB % 16 == 0, "TMA box rows / UMMA N granularity");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+  static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
 
   __device__ static uint32_t x_full(uint32_t base, int s) { return base + kOffBar + 8 * s; }
   __device__ static uint32_t x_empty(uint32_t base, int s) { return base + kOffBar + 8 * (MT + s); }
@@ -133,6 +155,15 @@ enum : int {
 __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err, int code) {
   *abort_flag = 1;
   atomicCAS(err, 0, code);
+}
+
+// Bounded wait by lane 0, result broadcast to the warp (the other lanes park in
+// the shuffle instead of spinning).
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, const volatile int* abort,
+                                          int lane, uint64_t deadline_ns = kWaitDeadlineNs) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait(bar, parity, abort, deadline_ns) ? 1 : 0;
+  return __shfl_sync(0xFFFFFFFFu, ok, 0) != 0;
 }
 
 // tcgen05.wait::ld that also "rewrites" the destination registers, so no use
@@ -215,31 +246,55 @@ __device__ __forceinline__ void merge_best(float m, int col0, float& best_val, i
       : "f"(mt), "r"(cand));
 }
 
-// Reads NCH accumulator columns of this thread's TMEM lane and folds them into
-// the running best. Loads of group g+1 are in flight while group g is reduced.
-template <int NCH, bool MASKED>
-__device__ __forceinline__ void epilogue_item(uint32_t taddr, int valid, int col0,
-                                              float& best_val, int& best_idx) {
-  constexpr int G = NCH / 32;
-  const uint32_t mask = 0xFFFFFFE0u;
-  uint32_t ra[32], rb[32];
-  tmem_ld_32x32b_x32(taddr, ra);
-  tmem_wait_ld_regs(ra);
+// Copies this thread's NCH accumulator columns (one TMEM lane) into registers:
+// all loads are issued back to back and waited for once, so the TMEM slot can be
+// handed back to the MMA before any of the reduction work.
+template <int NCH>
+__device__ __forceinline__ void epilogue_load(uint32_t taddr, uint32_t (&r)[NCH / 32][32]) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if ((g & 1) == 0) {
-      if (g + 1 < G) tmem_ld_32x32b_x32(taddr + (g + 1) * 32, rb);
-      merge_best(group_max<MASKED>(ra, mask, valid - g * 32), col0 + g * 32, best_val, best_idx);
-      if (g + 1 < G) tmem_wait_ld_regs(rb);
-    } else {
-      if (g + 1 < G) tmem_ld_32x32b_x32(taddr + (g + 1) * 32, ra);
-      merge_best(group_max<MASKED>(rb, mask, valid - g * 32), col0 + g * 32, best_val, best_idx);
-      if (g + 1 < G) tmem_wait_ld_regs(ra);
-    }
-  }
+  for (int g = 0; g < NCH / 32; ++g) tmem_ld_32x32b_x32(taddr + g * 32, r[g]);
+#pragma unroll
+  for (int g = 0; g < NCH / 32; ++g) tmem_wait_ld_regs(r[g]);
 }
 
-template <int DB, int MT, int NC, int ST, bool BF16>
+// Folds NCH columns (already in registers) into the running best.
+template <int NCH, bool MASKED>
+__device__ __forceinline__ void epilogue_reduce(const uint32_t (&r)[NCH / 32][32], int valid,
+                                                int col0, float& best_val, int& best_idx) {
+  const uint32_t mask = 0xFFFFFFE0u;
+#pragma unroll
+  for (int g = 0; g < NCH / 32; ++g)
+    merge_best(group_max<MASKED>(r[g], mask, valid - g * 32), col0 + g * 32, best_val, best_idx);
+}
+
+template <int CG>
+__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                         int c0, int c1, int c2) {
+  if constexpr (CG == 2)
+    tma_load_3d_cg2(dst, map, bar, c0, c1, c2);
+  else
+    tma_load_3d(dst, map, bar, c0, c1, c2);
+}
+
+template <int CG>
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                    uint32_t acc) {
+  if constexpr (CG == 2)
+    umma_f16_cg2(d, a, b, idesc, acc);
+  else
+    umma_f16(d, a, b, idesc, acc);
+}
+
+// MMA completion -> barrier `bar` of this CTA, and of the peer CTA for CG = 2.
+template <int CG>
+__device__ __forceinline__ void mma_done(uint32_t bar) {
+  if constexpr (CG == 2)
+    umma_commit_cg2_pair(bar, 0x3);
+  else
+    umma_commit(bar);
+}
+
+template <int DB, int MT, int NC, int ST, bool BF16, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     assign_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_aext,
@@ -247,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_cext, int32_t* __restrict__ ids,
                      int32_t* __restrict__ counts, int N, int K, int ksteps,
                      int tiles_per_batch, int total_tiles, int* __restrict__ err) {
-  using C = Cfg<DB, MT, NC, ST>;
+  using C = Cfg<DB, MT, NC, ST, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -257,6 +312,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Position in the CTA pair (0 for CG = 1); the even CTA issues the MMAs.
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  // Full barriers and the accumulator-release barriers live in the even CTA.
+  const uint32_t sb_lead = (CG == 2) ? mapa_shared(sb, 0) : sb;
+  // Tiles are processed by CTA pairs (CG = 2) or single CTAs.
+  const int unit = blockIdx.x / CG;
+  const int units = gridDim.x / CG;
+  const int rows_per_tile = CG * MT * kRowsPerSub;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < MT; ++s) {
@@ -269,11 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(C::acc_full(sb, a), 1);
-      mbar_init(C::acc_empty(sb, a), kEpiWarps);  // one arrival per epilogue warp
+      mbar_init(C::acc_empty(sb, a), CG * kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(C::drain(sb), 1);
-    mbar_init(C::merge_full(sb), kEpiWarps - 4);  // the warps of column parts 1..3
-    mbar_init(C::merge_empty(sb), 4);             // the four warps of part 0
+    mbar_init(C::merge_full(sb), kEpiWarps - 4);  // the warps of column slices 1..
+    mbar_init(C::merge_empty(sb), 4);             // the four warps of slice 0
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -284,89 +348,108 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_cext);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_cg2(smem_u32(tmem_holder), C::kTmemCols);
+      tmem_relinquish_cg2();
+    } else {
+      tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync();  // both CTAs' barriers initialised before any remote signal
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int nchunks = (K + NC - 1) / NC;
 
+  // The producer runs its loop with all 32 lanes on warp-uniform values (lane 0
+  // waits and issues the TMA loads); the MMA issuer is a single lane. (A warp-
+  // wide MMA loop was measured slower on B200: c3 assign 0.94 ms vs 0.90 ms.)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA
-    if (lane == 0) {
-      uint32_t c_it = 0, x_it = 0;
-      int c_last_ph[ST];
-      int x_last_ph[MT];
+    uint32_t c_it = 0, x_it = 0;
+    int c_last_ph[ST];
+    int x_last_ph[MT];
 #pragma unroll
-      for (int st = 0; st < ST; ++st) c_last_ph[st] = -1;
+    for (int st = 0; st < ST; ++st) c_last_ph[st] = -1;
 #pragma unroll
-      for (int s = 0; s < MT; ++s) x_last_ph[s] = -1;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-        const int b = tile / tiles_per_batch;
-        const int row0 = (tile - b * tiles_per_batch) * (MT * kRowsPerSub);
-        for (int ch = 0; ok && ch < nchunks; ++ch) {
-          const int st = static_cast<int>(c_it % ST);
-          const uint32_t ph = (c_it / ST) & 1u;
-          if (!mbar_wait(C::c_empty(sb, st), ph ^ 1u, abort_flag)) {
-            raise_abort(abort_flag, err, kErrProducerC);
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(C::c_full(sb, st), C::kCTxBytes);
+    for (int s = 0; s < MT; ++s) x_last_ph[s] = -1;
+    bool ok = true;
+    for (int tile = unit; ok && tile < total_tiles; tile += units) {
+      const int b = tile / tiles_per_batch;
+      const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
+                       static_cast<int>(rank) * MT * kRowsPerSub;
+      for (int ch = 0; ok && ch < nchunks; ++ch) {
+        const int st = static_cast<int>(c_it % ST);
+        const uint32_t ph = (c_it / ST) & 1u;
+        if (!warp_wait(C::c_empty(sb, st), ph ^ 1u, abort_flag, lane)) {
+          if (lane == 0) raise_abort(abort_flag, err, kErrProducerC);
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          if (leader) mbar_arrive_expect_tx(C::c_full(sb, st), C::kCTxBytes);
+          const uint32_t full = C::c_full(sb_lead, st);
+          const int crow = ch * NC + static_cast<int>(rank) * C::kNB;
 #pragma unroll
           for (int kb = 0; kb < DB; ++kb)
-            tma_load_3d(sb + C::kOffC + (st * DB + kb) * C::kCBlockBytes, &tm_c,
-                        C::c_full(sb, st), kb * kKBlockElems, ch * NC, b);
-          tma_load_3d(sb + C::kOffCext + st * C::kCextStageBytes, &tm_cext, C::c_full(sb, st),
-                      0, ch * NC, b);
-          c_last_ph[st] = static_cast<int>(ph);
-          ++c_it;
-          if (ch == 0) {
+            tma_load<CG>(sb + C::kOffC + (st * DB + kb) * C::kCBlockBytes, &tm_c, full,
+                         kb * kKBlockElems, crow, b);
+          tma_load<CG>(sb + C::kOffCext + st * C::kCextStageBytes, &tm_cext, full, 0, crow, b);
+        }
+        __syncwarp();
+        c_last_ph[st] = static_cast<int>(ph);
+        ++c_it;
+        if (ch == 0) {
 #pragma unroll
-            for (int s = 0; s < MT; ++s) {
-              if (!mbar_wait(C::x_empty(sb, s), (x_it & 1u) ^ 1u, abort_flag)) {
-                raise_abort(abort_flag, err, kErrProducerX);
-                ok = false;
-                break;
-              }
-              mbar_arrive_expect_tx(C::x_full(sb, s), C::kXTxBytes);
+          for (int s = 0; s < MT; ++s) {
+            if (!warp_wait(C::x_empty(sb, s), (x_it & 1u) ^ 1u, abort_flag, lane)) {
+              if (lane == 0) raise_abort(abort_flag, err, kErrProducerX);
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              if (leader) mbar_arrive_expect_tx(C::x_full(sb, s), C::kXTxBytes);
+              const uint32_t xfull = C::x_full(sb_lead, s);
 #pragma unroll
               for (int kb = 0; kb < DB; ++kb)
-                tma_load_3d(sb + C::kOffX + (s * DB + kb) * (kRowsPerSub * kKBlockBytes), &tm_x,
-                            C::x_full(sb, s), kb * kKBlockElems, row0 + s * kRowsPerSub, b);
-              tma_load_3d(sb + C::kOffAext + s * C::kAextSubBytes, &tm_aext, C::x_full(sb, s), 0,
-                          row0 + s * kRowsPerSub, b);
-              x_last_ph[s] = static_cast<int>(x_it & 1u);
+                tma_load<CG>(sb + C::kOffX + (s * DB + kb) * (kRowsPerSub * kKBlockBytes), &tm_x,
+                             xfull, kb * kKBlockElems, row0 + s * kRowsPerSub, b);
+              tma_load<CG>(sb + C::kOffAext + s * C::kAextSubBytes, &tm_aext, xfull, 0,
+                           row0 + s * kRowsPerSub, b);
             }
+            __syncwarp();
+            x_last_ph[s] = static_cast<int>(x_it & 1u);
           }
         }
-        ++x_it;
       }
-      if (!ok) {
-        // Let every load already issued land before the CTA can exit.
+      ++x_it;
+    }
+    if (!ok && leader && lane == 0) {
+      // Let every load already issued land before the CTA can exit (the
+      // completions of both CTAs are counted on the even CTA's barriers).
 #pragma unroll
-        for (int st = 0; st < ST; ++st)
-          if (c_last_ph[st] >= 0)
-            mbar_wait(C::c_full(sb, st), static_cast<uint32_t>(c_last_ph[st]), abort_flag,
-                      100000000ull);
+      for (int st = 0; st < ST; ++st)
+        if (c_last_ph[st] >= 0)
+          mbar_wait(C::c_full(sb, st), static_cast<uint32_t>(c_last_ph[st]), abort_flag,
+                    100000000ull);
 #pragma unroll
-        for (int s = 0; s < MT; ++s)
-          if (x_last_ph[s] >= 0)
-            mbar_wait(C::x_full(sb, s), static_cast<uint32_t>(x_last_ph[s]), abort_flag,
-                      100000000ull);
-      }
+      for (int s = 0; s < MT; ++s)
+        if (x_last_ph[s] >= 0)
+          mbar_wait(C::x_full(sb, s), static_cast<uint32_t>(x_last_ph[s]), abort_flag,
+                    100000000ull);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc_f16(BF16 ? 1u : 0u, kRowsPerSub, NC);
-      const uint32_t idesc_ext = umma_idesc_f16(1u, kRowsPerSub, NC);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = umma_idesc_f16(BF16 ? 1u : 0u, CG * kRowsPerSub, NC);
+      const uint32_t idesc_ext = umma_idesc_f16(1u, CG * kRowsPerSub, NC);
       uint32_t c_it = 0, x_it = 0, item = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int tile = unit; ok && tile < total_tiles; tile += units) {
         for (int ch = 0; ok && ch < nchunks; ++ch) {
           const int st = static_cast<int>(c_it % ST);
           const uint32_t ph = (c_it / ST) & 1u;
@@ -398,35 +481,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                   x_sub + koff * (kRowsPerSub * kKBlockBytes) + kin, 1024, kLayoutSwizzle128B);
               const uint64_t b_desc =
                   umma_smem_desc(c_stage + koff * C::kCBlockBytes + kin, 1024, kLayoutSwizzle128B);
-              umma_f16(d_tmem, a_desc, b_desc, idesc, ks > 0 ? 1u : 0u);
+              mma<CG>(d_tmem, a_desc, b_desc, idesc, ks > 0 ? 1u : 0u);
             }
             const uint64_t ae = umma_smem_desc(sb + C::kOffAext + s * C::kAextSubBytes, 256,
                                                kLayoutSwizzle32B);
             const uint64_t be = umma_smem_desc(sb + C::kOffCext + st * C::kCextStageBytes, 256,
                                                kLayoutSwizzle32B);
-            umma_f16(d_tmem, ae, be, idesc_ext, 1u);
-            umma_commit(C::acc_full(sb, slot));
-            if (ch == nchunks - 1) umma_commit(C::x_empty(sb, s));
+            mma<CG>(d_tmem, ae, be, idesc_ext, 1u);
+            mma_done<CG>(C::acc_full(sb, slot));
+            if (ch == nchunks - 1) mma_done<CG>(C::x_empty(sb, s));
             ++item;
           }
-          umma_commit(C::c_empty(sb, st));
+          mma_done<CG>(C::c_empty(sb, st));
           ++c_it;
         }
         ++x_it;
       }
       // Every MMA issued above has completed once this commit arrives.
-      umma_commit(C::drain(sb));
+      if constexpr (CG == 2)
+        umma_commit_cg2_pair(C::drain(sb), 0x1);
+      else
+        umma_commit(C::drain(sb));
       mbar_wait(C::drain(sb), 0u, abort_flag, ok ? kWaitDeadlineNs : 100000000ull);
     }
   } else {
     // ----------------------------------------------------------- epilogue
-    // kParts warpgroups: part p reads columns [p*NCP, (p+1)*NCP) of every item
-    // for all 128 TMEM lanes (one x row per thread). At the end of a tile parts
-    // 1.. hand their per-row best to part 0 through shared memory (bounded
-    // mbarrier handshake) and part 0 writes the labels.
-    constexpr int kParts = kEpiWarps / 4;
+    // kParts warpgroups: slice p reads columns [p*NCH, (p+1)*NCH) of every item
+    // for all 128 TMEM lanes (one x row per thread). At the end of a tile the
+    // slices 1.. hand their per-row best to slice 0 through shared memory
+    // (bounded mbarrier handshake) and slice 0 writes the labels.
     constexpr int NCH = NC / kParts;
-    static_assert(NCH % 32 == 0, "each epilogue part reads whole 32-column groups");
+    static_assert(NCH % 32 == 0, "each epilogue slice reads whole 32-column groups");
     const int epi = warp - kEpiWarpBegin;
     const int part = epi >> 2;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -438,9 +523,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         reinterpret_cast<int*>(smem + C::kOffMerge + (kParts - 1) * MT * kRowsPerSub * 4);
     uint32_t item = 0, tcount = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++tcount) {
+    for (int tile = unit; ok && tile < total_tiles; tile += units, ++tcount) {
       const int b = tile / tiles_per_batch;
-      const int row0 = (tile - b * tiles_per_batch) * (MT * kRowsPerSub);
+      const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
+                       static_cast<int>(rank) * MT * kRowsPerSub;
       float best_val[MT];
       int best_idx[MT];
 #pragma unroll
@@ -463,14 +549,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t taddr = lane_addr + slot * NC;
-          if (valid >= NCH)
-            epilogue_item<NCH, false>(taddr, valid, col0, best_val[s], best_idx[s]);
-          else if (valid > 0)
-            epilogue_item<NCH, true>(taddr, valid, col0, best_val[s], best_idx[s]);
+          uint32_t r[NCH / 32][32];
+          if (valid > 0) epilogue_load<NCH>(lane_addr + slot * NC, r);
+          // The slot's columns are in registers: release it to the MMA now.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(C::acc_empty(sb, slot));
+          if (lane == 0) {
+            if constexpr (CG == 2)
+              mbar_arrive_cluster(C::acc_empty(sb_lead, slot));
+            else
+              mbar_arrive(C::acc_empty(sb, slot));
+          }
+          if (valid >= NCH)
+            epilogue_reduce<NCH, false>(r, valid, col0, best_val[s], best_idx[s]);
+          else if (valid > 0)
+            epilogue_reduce<NCH, true>(r, valid, col0, best_val[s], best_idx[s]);
           ++item;
         }
       }
@@ -533,87 +626,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  __syncthreads();
+  // No remote signal may target a CTA that has exited: the pair leaves together.
+  if constexpr (CG == 2)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::kTmemCols);
+    if constexpr (CG == 2)
+      tmem_dealloc_cg2(tmem_base, C::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, C::kTmemCols);
   }
 }
 
-// Sum of squares of one row, one warp. 16-byte vector loads when the row
-// length allows it, scalar loads otherwise.
-template <typename T>
-__device__ __forceinline__ float warp_row_sumsq(const T* row, int D, int lane) {
-  constexpr int kVec = 16 / sizeof(T);
-  float acc = 0.f;
-  if ((D * sizeof(T)) % 16 == 0) {
-    for (int v = lane; v * kVec < D; v += 32) {
-      const uint4 u = reinterpret_cast<const uint4*>(row)[v];
-      const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-      for (int i = 0; i < kVec; ++i) {
-        const float f = to_f32<T>(e[i]);
-        acc = fmaf(f, f, acc);
-      }
-    }
-  } else {
-    for (int d = lane; d < D; d += 32) {
-      const float f = to_f32<T>(row[d]);
-      acc = fmaf(f, f, acc);
-    }
-  }
-  return warp_sum(acc);
+// FKC_ASSIGN_CTA_GROUP=2 selects the CTA-pair kernel; default: single CTAs,
+// which measured faster on B200 at every benchmark shape (assign ms, CG=1 vs
+// CG=2: c3 0.90 vs 1.04, c2 0.073 vs 0.090, c4 0.130 vs 0.162). The pair
+// kernel halves operand traffic per SM, but the epilogue, not operand
+// bandwidth, bounds this kernel, and the pair's cross-CTA handshakes add
+// latency to every accumulator slot.
+int cta_group_choice() {
+  static const int v = [] {
+    const char* s = std::getenv("FKC_ASSIGN_CTA_GROUP");
+    return (s != nullptr && std::strcmp(s, "2") == 0) ? 2 : 1;
+  }();
+  return v;
 }
 
-template <typename T>
-__global__ void xnorm_ext_kernel(const T* __restrict__ x, uint8_t* __restrict__ aext,
-                                 int64_t rows, int D) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       r < rows; r += warps_total) {
-    const float s = warp_row_sumsq<T>(x + r * D, D, lane);
-    if (lane == 0) write_norm_ext(aext + r * kExtBytes, -0.5f * s, true);
-  }
-}
-
-// Centroid terms: the norm-extension row (cext, nullable) and ||c||^2 (c_sq_out,
-// nullable). The squared norm is taken from c_sq when given (the caller's
-// value, as the reference's raw-distance path does), else computed from c.
-template <typename T>
-__global__ void cnorm_ext_kernel(const T* __restrict__ c, const float* __restrict__ c_sq,
-                                 uint8_t* __restrict__ cext, float* __restrict__ c_sq_out,
-                                 int64_t rows, int D) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       r < rows; r += warps_total) {
-    const float s = (c_sq != nullptr) ? c_sq[r] : warp_row_sumsq<T>(c + r * D, D, lane);
-    if (lane == 0) {
-      if (cext != nullptr) write_norm_ext(cext + r * kExtBytes, -0.5f * s, false);
-      if (c_sq_out != nullptr) c_sq_out[r] = s;
-    }
-  }
-}
-
-int grid_for_rows(int64_t rows, int warps_per_block) {
-  const DeviceInfo* di = nullptr;
-  int sms = 148;
-  if (current_device_info(&di) == FKC_OK) sms = di->sm_count;
-  int64_t blocks = (rows + warps_per_block - 1) / warps_per_block;
-  const int64_t cap = static_cast<int64_t>(sms) * 16;
-  if (blocks > cap) blocks = cap;
-  if (blocks < 1) blocks = 1;
-  return static_cast<int>(blocks);
-}
-
-template <int DB, int MT, int NC, int ST, bool BF16>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG>
 int launch_tc_impl(const void* x, const void* centroids, const void* aext, const void* cext,
                    int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
                    cudaStream_t stream) {
-  using C = Cfg<DB, MT, NC, ST>;
-  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16>;
+  using C = Cfg<DB, MT, NC, ST, CG>;
+  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG>;
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   FKC_CUDA_TRY(
@@ -627,41 +674,83 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
                          CU_TENSOR_MAP_SWIZZLE_128B));
   FKC_TRY(encode_tmap_3d(&tm_aext, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, aext, 16, N, B, kExtBytes,
                          N * kExtBytes, 16, kRowsPerSub, CU_TENSOR_MAP_SWIZZLE_32B));
-  FKC_TRY(encode_tmap_3d(&tm_c, tdt, centroids, D, K, B, D * es, K * D * es, kKBlockElems, NC,
-                         CU_TENSOR_MAP_SWIZZLE_128B));
+  FKC_TRY(encode_tmap_3d(&tm_c, tdt, centroids, D, K, B, D * es, K * D * es, kKBlockElems,
+                         C::kNB, CU_TENSOR_MAP_SWIZZLE_128B));
   FKC_TRY(encode_tmap_3d(&tm_cext, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cext, 16, K, B, kExtBytes,
-                         K * kExtBytes, 16, NC, CU_TENSOR_MAP_SWIZZLE_32B));
+                         K * kExtBytes, 16, C::kNB, CU_TENSOR_MAP_SWIZZLE_32B));
 
-  const int64_t rows_per_tile = static_cast<int64_t>(MT) * kRowsPerSub;
+  const int64_t rows_per_tile = static_cast<int64_t>(CG) * MT * kRowsPerSub;
   const int64_t tiles_per_batch = (N + rows_per_tile - 1) / rows_per_tile;
   const int64_t total_tiles = tiles_per_batch * B;
   FKC_REQUIRE(total_tiles < (1ll << 31), "assign: too many row tiles (%lld)",
               static_cast<long long>(total_tiles));
-  const int grid = static_cast<int>(std::min<int64_t>(total_tiles, di->sm_count));
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(
-      tm_x, tm_aext, tm_c, tm_cext, ids, counts, static_cast<int>(N), static_cast<int>(K),
-      static_cast<int>(D / 16), static_cast<int>(tiles_per_batch), static_cast<int>(total_tiles),
-      device_error_word());
-  FKC_CUDA_TRY(cudaGetLastError());
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  int units = di->sm_count;
+  if constexpr (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Number of CTA pairs the device can hold at once (a persistent grid must
+    // not exceed it: pairs beyond it would wait for a second wave).
+    static int pairs_cached[64] = {};
+    int& pairs = pairs_cached[di->device & 63];
+    if (pairs == 0) {
+      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+      int clusters = 0;
+      FKC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+      pairs = clusters > 0 ? clusters : -1;
+    }
+    FKC_REQUIRE(pairs > 0, "assign: this device cannot co-schedule 2-CTA clusters");
+    units = pairs;
+  }
+  const int64_t n_units = std::min<int64_t>(total_tiles, units);
+  cfg.gridDim = dim3(static_cast<unsigned>(CG * n_units), 1, 1);
+  FKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tm_x, tm_aext, tm_c, tm_cext, ids, counts,
+                                  static_cast<int>(N), static_cast<int>(K),
+                                  static_cast<int>(D / 16), static_cast<int>(tiles_per_batch),
+                                  static_cast<int>(total_tiles), device_error_word()));
   count_launches(1);
   return FKC_OK;
 }
 
-template <bool BF16>
+template <bool BF16, int CG>
 int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, const void* cext,
                        int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
                        cudaStream_t stream) {
-  if (D <= 64)
-    return launch_tc_impl<1, 2, 256, 4, BF16>(x, centroids, aext, cext, ids, counts, B, N, K, D,
-                                              stream);
-  if (D <= 128)
-    return launch_tc_impl<2, 2, 256, 2, BF16>(x, centroids, aext, cext, ids, counts, B, N, K, D,
-                                              stream);
-  if (D <= 192)
-    return launch_tc_impl<3, 2, 128, 2, BF16>(x, centroids, aext, cext, ids, counts, B, N, K, D,
-                                              stream);
-  return launch_tc_impl<4, 1, 128, 2, BF16>(x, centroids, aext, cext, ids, counts, B, N, K, D,
-                                            stream);
+  // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
+  if constexpr (CG == 2) {
+    if (D <= 64)
+      return launch_tc_impl<1, 2, 256, 8, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    if (D <= 128)
+      return launch_tc_impl<2, 2, 256, 4, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    if (D <= 192)
+      return launch_tc_impl<3, 2, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    return launch_tc_impl<4, 1, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N, K,
+                                                 D, stream);
+  } else {
+    if (D <= 64)
+      return launch_tc_impl<1, 2, 256, 4, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    if (D <= 128)
+      return launch_tc_impl<2, 2, 256, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    if (D <= 192)
+      return launch_tc_impl<3, 2, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+                                                   K, D, stream);
+    return launch_tc_impl<4, 1, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N, K,
+                                                 D, stream);
+  }
 }
 
 }  // namespace
@@ -674,57 +763,21 @@ bool assign_tc_supported(int64_t D, int dtype) {
   return di->cc_major == 10 && di->smem_optin >= static_cast<size_t>(kSmemLimit);
 }
 
-int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D, int dtype,
-                     cudaStream_t stream) {
-  const int64_t rows = B * N;
-  const int grid = grid_for_rows(rows, 8);
-  if (dtype == FKC_DTYPE_BF16)
-    xnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(aext), rows,
-        static_cast<int>(D));
-  else
-    xnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(
-        static_cast<const __half*>(x), static_cast<uint8_t*>(aext), rows, static_cast<int>(D));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
-}
-
-int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
-                     int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream) {
-  const int64_t rows = B * K;
-  const int grid = grid_for_rows(rows, 8);
-  uint8_t* ce = static_cast<uint8_t*>(cext);
-  const int d = static_cast<int>(D);
-  switch (dtype) {
-    case FKC_DTYPE_BF16:
-      cnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(centroids), c_sq, ce, c_sq_out, rows, d);
-      break;
-    case FKC_DTYPE_F16:
-      cnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(centroids),
-                                                         c_sq, ce, c_sq_out, rows, d);
-      break;
-    case FKC_DTYPE_F32:
-      cnorm_ext_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(centroids),
-                                                        c_sq, ce, c_sq_out, rows, d);
-      break;
-    default:
-      return set_error(FKC_EINVAL, "bad dtype %d", dtype);
-  }
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
-}
-
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
                      int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
                      int dtype, cudaStream_t stream) {
   FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
               static_cast<long long>(D), dtype);
-  if (dtype == FKC_DTYPE_BF16)
-    return launch_tc_dispatch<true>(x, centroids, aext, cext, ids, counts, B, N, K, D, stream);
-  return launch_tc_dispatch<false>(x, centroids, aext, cext, ids, counts, B, N, K, D, stream);
+  const bool bf16 = dtype == FKC_DTYPE_BF16;
+  if (cta_group_choice() == 2)
+    return bf16 ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+                                              stream)
+                : launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+                                               stream);
+  return bf16 ? launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+                                            stream)
+              : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+                                             stream);
 }
 
 }  // namespace fkc

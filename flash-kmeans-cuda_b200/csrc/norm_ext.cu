@@ -1,0 +1,128 @@
+// Norm-extension rows read by the tcgen05 assignment kernel (one extra K=16
+// slice of bf16 operands that folds the squared norms into the MMA, see
+// assign_tc.cu): per point {h1,h2,h3,1,1,1,-delta,0...} with h1+h2+h3 =
+// -||x||^2/2, per centroid {1,1,1,h1,h2,h3,1,0...} with h = -||c||^2/2.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "fkc_common.cuh"
+#include "fkc_internal.h"
+
+namespace fkc {
+namespace {
+
+constexpr int kExtBytes = kNormExtBytes;
+
+// Sum of squares of one row, one warp. 16-byte vector loads when the row
+// length allows it, scalar loads otherwise.
+template <typename T>
+__device__ __forceinline__ float warp_row_sumsq(const T* row, int D, int lane) {
+  constexpr int kVec = 16 / sizeof(T);
+  float acc = 0.f;
+  if ((D * sizeof(T)) % 16 == 0) {
+    for (int v = lane; v * kVec < D; v += 32) {
+      const uint4 u = reinterpret_cast<const uint4*>(row)[v];
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        const float f = to_f32<T>(e[i]);
+        acc = fmaf(f, f, acc);
+      }
+    }
+  } else {
+    for (int d = lane; d < D; d += 32) {
+      const float f = to_f32<T>(row[d]);
+      acc = fmaf(f, f, acc);
+    }
+  }
+  return warp_sum(acc);
+}
+
+template <typename T>
+__global__ void xnorm_ext_kernel(const T* __restrict__ x, uint8_t* __restrict__ aext,
+                                 int64_t rows, int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < rows; r += warps_total) {
+    const float s = warp_row_sumsq<T>(x + r * D, D, lane);
+    if (lane == 0) write_norm_ext(aext + r * kExtBytes, -0.5f * s, true);
+  }
+}
+
+// Centroid terms: the norm-extension row (cext, nullable) and ||c||^2 (c_sq_out,
+// nullable). The squared norm is taken from c_sq when given (the caller's
+// value, as the reference's raw-distance path does), else computed from c.
+template <typename T>
+__global__ void cnorm_ext_kernel(const T* __restrict__ c, const float* __restrict__ c_sq,
+                                 uint8_t* __restrict__ cext, float* __restrict__ c_sq_out,
+                                 int64_t rows, int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < rows; r += warps_total) {
+    const float s = (c_sq != nullptr) ? c_sq[r] : warp_row_sumsq<T>(c + r * D, D, lane);
+    if (lane == 0) {
+      if (cext != nullptr) write_norm_ext(cext + r * kExtBytes, -0.5f * s, false);
+      if (c_sq_out != nullptr) c_sq_out[r] = s;
+    }
+  }
+}
+
+int grid_for_rows(int64_t rows, int warps_per_block) {
+  const DeviceInfo* di = nullptr;
+  int sms = 148;
+  if (current_device_info(&di) == FKC_OK) sms = di->sm_count;
+  int64_t blocks = (rows + warps_per_block - 1) / warps_per_block;
+  const int64_t cap = static_cast<int64_t>(sms) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+}  // namespace
+
+int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D, int dtype,
+                     cudaStream_t stream) {
+  const int64_t rows = B * N;
+  const int grid = grid_for_rows(rows, 8);
+  if (dtype == FKC_DTYPE_BF16)
+    xnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(aext), rows,
+        static_cast<int>(D));
+  else
+    xnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(
+        static_cast<const __half*>(x), static_cast<uint8_t*>(aext), rows, static_cast<int>(D));
+  FKC_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
+  return FKC_OK;
+}
+
+int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
+                     int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream) {
+  const int64_t rows = B * K;
+  const int grid = grid_for_rows(rows, 8);
+  uint8_t* ce = static_cast<uint8_t*>(cext);
+  const int d = static_cast<int>(D);
+  switch (dtype) {
+    case FKC_DTYPE_BF16:
+      cnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(centroids), c_sq, ce, c_sq_out, rows, d);
+      break;
+    case FKC_DTYPE_F16:
+      cnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(centroids),
+                                                         c_sq, ce, c_sq_out, rows, d);
+      break;
+    case FKC_DTYPE_F32:
+      cnorm_ext_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(centroids),
+                                                        c_sq, ce, c_sq_out, rows, d);
+      break;
+    default:
+      return set_error(FKC_EINVAL, "bad dtype %d", dtype);
+  }
+  FKC_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
+  return FKC_OK;
+}
+
+}  // namespace fkc

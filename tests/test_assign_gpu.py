@@ -148,3 +148,44 @@ def test_out_buffer_and_errors(cuda_device):
         _C.euclid_assign(x, c.float(), x_sq, (c.float() ** 2).sum(-1), None)
     with pytest.raises(ValueError):
         euclid_assign(x.cpu(), c, x_sq)
+
+
+_PAIR_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path[:0] = sys.argv[2:4]
+from _data import iid, subset_init
+from flash_kmeans_cuda import _C
+out = {}
+for i, (B, N, K, D, dt) in enumerate(eval(sys.argv[4])):
+    x = iid(B, N, D, seed=B * 7 + N + K + D, dtype=dt)
+    c = subset_init(x, K, seed=1) if K <= N else iid(B, K, D, seed=3, dtype=dt)
+    xd, cd = x.cuda(), c.cuda()
+    ids = _C.euclid_assign(xd, cd, (xd.float() ** 2).sum(-1), (cd.float() ** 2).sum(-1), None)
+    out[f"ids{i}"] = ids.cpu().numpy()
+np.savez(sys.argv[1], **out)
+"""
+
+PAIR_SHAPES = [(1, 1024, 64, 64, "float16"), (2, 8192, 256, 128, "bfloat16"),
+               (1, 777, 513, 192, "float16"), (1, 1024, 32, 256, "bfloat16"),
+               (1, 4100, 1000, 128, "float16")]
+
+
+def test_cta_pair_kernel_matches_oracle(cuda_device, tmp_path):
+    """The opt-in CTA-pair (cta_group::2) kernel, in a fresh process with
+    FKC_ASSIGN_CTA_GROUP=2 (the choice is read once per process)."""
+    import os
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    pkg = os.path.join(os.path.dirname(here), "flash-kmeans-cuda_b200")
+    out = tmp_path / "pair.npz"
+    env = dict(os.environ, FKC_ASSIGN_CTA_GROUP="2")
+    r = subprocess.run([sys.executable, "-c", _PAIR_SCRIPT, str(out), here, pkg,
+                        repr(PAIR_SHAPES)], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    got = np.load(out)
+    for i, (B, N, K, D, dt) in enumerate(PAIR_SHAPES):
+        x = iid(B, N, D, seed=B * 7 + N + K + D, dtype=dt)
+        c = subset_init(x, K, seed=1) if K <= N else iid(B, K, D, seed=3, dtype=dt)
+        _check(got[f"ids{i}"], orc.assign(to_np(x), to_np(c)), f"pair {dt} {B}x{N}x{K}x{D}")
