@@ -39,6 +39,8 @@ _SIGNATURES = {
     "fkc_assign_workspace_size": (c_size, [c_i64, c_i64, c_i64, c_i64, c_int]),
     "fkc_assign": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_int,
                            c_vp, c_size, c_vp]),
+    "fkc_assign_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                   c_int, c_vp]),
     "fkc_update_sorted": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_int,
                                   c_vp]),
     "fkc_update_sorted_indexed": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,

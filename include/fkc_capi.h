@@ -94,6 +94,30 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
                                fkc_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Assignment without a workspace and without device allocation. No
+ * counterpart in the reference (which allocates through torch); added for
+ * callers that cannot allocate device memory: FFI bindings of the 5-argument
+ * euclid_assign signature that only receive device pointers, hosts whose
+ * device memory a pooling allocator has reserved, and latency-critical
+ * pipelines that cannot take cudaFree's device-wide synchronisation.
+ *   Same arguments, results and errors as fkc_assign minus the workspace.
+ *   Scratch: a static device array of FKC_ASSIGN_NOALLOC_SCRATCH_BYTES per
+ *   device (32 MiB), needed on the tensor-core path only. A call needing more
+ *   than that, i.e. fkc_assign_workspace_size() > the limit (about
+ *   B*N + B*K > 1,048,000 rows), returns FKC_EWORKSPACE with a message and
+ *   launches nothing.
+ *   The first call on each device looks up the scratch address on that device
+ *   (a set-up step): make that first call before any stream capture.
+ *   All calls on a device share the scratch: calls that overlap on the GPU
+ *   (unordered streams, concurrent host threads) race. Order them.
+ *   Allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ * ---------------------------------------------------------------------- */
+#define FKC_ASSIGN_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+FKC_CAPI_EXPORT int fkc_assign_noalloc(const void* x, const void* centroids, const float* x_sq,
+                                       const float* c_sq, int32_t* ids, int64_t B, int64_t N,
+                                       int64_t K, int64_t D, int dtype, fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Sorted-run accumulators with the reference _C semantics: they ADD into
  * caller-initialised sums (B,K,D) fp32 and counts (B,K) int32.
  *   ids_sorted (B,N): labels sorted ascending along N.

@@ -94,3 +94,17 @@ def test_device_queries_without_gpu():
         pytest.skip("host has a GPU")
     assert _lib.lib.fkc_device_supported() == 0
     assert _lib.lib.fkc_kernel_launches() == 0
+
+
+def test_noalloc_rejects_oversize_before_any_cuda_call():
+    """fkc_assign_noalloc checks its static-scratch limit on the host first."""
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    limit = 32 * 1024 * 1024
+    assert L.fkc_assign_workspace_size(1, limit // 32 - 8192, 8192, 64, 0) == limit
+    st = L.fkc_assign_noalloc(1, 1, None, None, 1, 1, limit // 32 - 8192 + 1, 8192, 64, 0, None)
+    assert st == -5 and "static scratch" in _lib.last_error()
+    # shapes of the CUDA-core kernel need no scratch: the limit does not apply
+    st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 64, 2, None)
+    assert st == -1 and "non-null" in _lib.last_error()
