@@ -48,12 +48,12 @@
 // even CTA issues tcgen05.mma.cta_group::2 with M = 256 (128 rows from each
 // CTA's shared memory) and N = 256 (128 centroids from each), and every CTA's
 // TMEM receives its own 128 rows x 256 columns. Per SM this halves the shared-
-// memory operand traffic of the MMA and the L2 reads of centroid chunks, which
-// bound the single-CTA kernel (CG = 1). TMA completions of both CTAs land on
-// the even CTA's full barriers; MMA completions are fanned out to both CTAs'
-// barriers by one commit with a CTA mask; the odd CTA's epilogue releases
-// accumulator slots with a remote arrive on the even CTA's barrier. Opt-in
-// (FKC_ASSIGN_CTA_GROUP=2): single CTAs are faster here (cta_group_choice).
+// memory operand traffic of the MMA and the L2 reads of centroid chunks. TMA
+// completions of both CTAs land on the even CTA's full barriers; MMA
+// completions are fanned out to both CTAs' barriers by one commit with a CTA
+// mask; the odd CTA's epilogue releases accumulator slots with a relaxed remote
+// arrive on the even CTA's barrier. Opt-in (FKC_ASSIGN_CTA_GROUP=2): it measured
+// no faster than single CTAs (cta_group_choice).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -447,6 +447,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && leader) {
       const uint32_t idesc = umma_idesc_f16(BF16 ? 1u : 0u, CG * kRowsPerSub, NC);
       const uint32_t idesc_ext = umma_idesc_f16(1u, CG * kRowsPerSub, NC);
+      constexpr uint32_t kHi128 = umma_desc_hi(1024, kLayoutSwizzle128B);
+      constexpr uint32_t kHi32 = umma_desc_hi(256, kLayoutSwizzle32B);
       uint32_t c_it = 0, x_it = 0, item = 0;
       bool ok = true;
       for (int tile = unit; ok && tile < total_tiles; tile += units) {
@@ -474,20 +476,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + slot * NC;
-            const uint32_t x_sub = sb + C::kOffX + s * C::kXSubBytes;
-            for (int ks = 0; ks < ksteps; ++ks) {
-              const uint32_t koff = (ks >> 2), kin = (ks & 3) * 32;
-              const uint64_t a_desc = umma_smem_desc(
-                  x_sub + koff * (kRowsPerSub * kKBlockBytes) + kin, 1024, kLayoutSwizzle128B);
-              const uint64_t b_desc =
-                  umma_smem_desc(c_stage + koff * C::kCBlockBytes + kin, 1024, kLayoutSwizzle128B);
-              mma<CG>(d_tmem, a_desc, b_desc, idesc, ks > 0 ? 1u : 0u);
+            // Few instructions per MMA: this lane shares its SM sub-partition
+            // with two epilogue warps, and every issue slot it needs is one
+            // they compete for (measured: the MMA stream slows by the
+            // epilogue work of this sub-partition alone).
+            const uint32_t a_lo = umma_desc_lo(sb + C::kOffX + s * C::kXSubBytes);
+            const uint32_t b_lo = umma_desc_lo(c_stage);
+#pragma unroll
+            for (int ks = 0; ks < DB * 4; ++ks) {
+              if (ks < ksteps) {
+                // K step of 16 elements = 32 bytes = 2 start units; a 64-element
+                // swizzle block is block_bytes / 16 units further.
+                constexpr uint32_t kStepA = (kRowsPerSub * kKBlockBytes) >> 4;
+                constexpr uint32_t kStepB = C::kCBlockBytes >> 4;
+                const uint32_t da = (ks >> 2) * kStepA + (ks & 3) * 2;
+                const uint32_t db = (ks >> 2) * kStepB + (ks & 3) * 2;
+                // Opaque to the compiler: the first step's "overwrite" flag stays
+                // a runtime predicate.
+                uint32_t accf = ks > 0 ? 1u : 0u;
+                asm volatile("" : "+r"(accf));
+                mma<CG>(d_tmem, umma_desc(a_lo + da, kHi128), umma_desc(b_lo + db, kHi128),
+                        idesc, accf);
+              }
             }
-            const uint64_t ae = umma_smem_desc(sb + C::kOffAext + s * C::kAextSubBytes, 256,
-                                               kLayoutSwizzle32B);
-            const uint64_t be = umma_smem_desc(sb + C::kOffCext + st * C::kCextStageBytes, 256,
-                                               kLayoutSwizzle32B);
-            mma<CG>(d_tmem, ae, be, idesc_ext, 1u);
+            mma<CG>(d_tmem, umma_desc(umma_desc_lo(sb + C::kOffAext + s * C::kAextSubBytes), kHi32),
+                    umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
+                    idesc_ext, 1u);
             mma_done<CG>(C::acc_full(sb, slot));
             if (ch == nchunks - 1) mma_done<CG>(C::x_empty(sb, s));
             ++item;
@@ -555,10 +569,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            if constexpr (CG == 2)
-              mbar_arrive_cluster(C::acc_empty(sb_lead, slot));
-            else
+            // Only "TMEM read done" is signalled (tcgen05.wait::ld above): the
+            // even CTA arrives locally, the odd one remotely with relaxed
+            // semantics (measured: a release arrive at cluster scope made the
+            // pair kernel 20% slower).
+            if (CG == 1 || leader)
               mbar_arrive(C::acc_empty(sb, slot));
+            else
+              mbar_arrive_cluster_relaxed(C::acc_empty(sb_lead, slot));
           }
           if (valid >= NCH)
             epilogue_reduce<NCH, false>(r, valid, col0, best_val[s], best_idx[s]);
@@ -642,11 +660,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // FKC_ASSIGN_CTA_GROUP=2 selects the CTA-pair kernel; default: single CTAs,
-// which measured faster on B200 at every benchmark shape (assign ms, CG=1 vs
-// CG=2: c3 0.90 vs 1.04, c2 0.073 vs 0.090, c4 0.130 vs 0.162). The pair
-// kernel halves operand traffic per SM, but the epilogue, not operand
-// bandwidth, bounds this kernel, and the pair's cross-CTA handshakes add
-// latency to every accumulator slot.
+// which measured as fast or faster on B200 (assign ms, CG=1 vs CG=2: c3 0.831
+// vs 0.827, c2 0.068 vs 0.072, c4 0.117 vs 0.130). The pair kernel halves the
+// L2 reads of centroid chunks per SM, but both are bound by the MMA stream and
+// the epilogue warps that share its SM sub-partition, and the pair adds a
+// cross-CTA handshake to every accumulator slot.
 int cta_group_choice() {
   static const int v = [] {
     const char* s = std::getenv("FKC_ASSIGN_CTA_GROUP");

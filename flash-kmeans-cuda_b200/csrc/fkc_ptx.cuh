@@ -218,9 +218,12 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
-// Arrive on an mbarrier given by a shared::cluster address (possibly the peer's).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+// Arrive on an mbarrier given by a shared::cluster address (possibly the peer's)
+// with relaxed semantics: it publishes no memory writes, only that this thread
+// has passed the arrive (e.g. its tcgen05.ld reads have completed). A release
+// arrive at cluster scope costs several hundred cycles per call on B200.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 
@@ -293,6 +296,22 @@ __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t start, uint32_t sbo_
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;  // bits [32,46)
   d |= static_cast<uint64_t>(1u) << 46;                        // descriptor version (sm_100)
   d |= static_cast<uint64_t>(layout & 7u) << 61;               // swizzle mode
+  return d;
+}
+
+// The same descriptor as two 32-bit halves, for issue loops that step the start
+// address: lo carries the start field (+ LBO), hi the SBO, version and layout.
+// Adding n to lo moves the start by 16*n bytes; the caller keeps the stepped
+// address inside shared memory, so the 14-bit field does not overflow.
+__device__ __forceinline__ uint32_t umma_desc_lo(uint32_t start) {
+  return ((start >> 4) & 0x3FFFu) | (1u << 16);
+}
+__host__ __device__ constexpr uint32_t umma_desc_hi(uint32_t sbo_bytes, uint32_t layout) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | ((layout & 7u) << 29);
+}
+__device__ __forceinline__ uint64_t umma_desc(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
   return d;
 }
 
