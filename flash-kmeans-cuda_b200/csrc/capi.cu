@@ -199,6 +199,8 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
   return FKC_OK;
 }
 
+// counts_ready: counts already holds the histogram of `ids` (fkc_lloyd_assign),
+// whose labels all lie in [0,K).
 int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* counts,
                     bool counts_ready, const UpdateWorkspace& uw, int64_t B, int64_t N,
                     int64_t K, int64_t D, int dtype, cudaStream_t st) {
@@ -206,7 +208,7 @@ int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* cou
     FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
     FKC_TRY(launch_histogram(ids, counts, B, N, K, st));
   }
-  FKC_TRY(launch_counting_sort(ids, counts, uw, B, N, K, st));
+  FKC_TRY(launch_counting_sort(ids, counts, uw, B, N, K, counts_ready, st));
   FKC_CUDA_TRY(cudaMemsetAsync(sums, 0, static_cast<size_t>(B * K * D) * 4, st));
   return launch_run_accumulate(x, uw.perm, uw.ids_sorted, sums, nullptr, B, N, K, D, dtype, st);
 }

@@ -103,10 +103,14 @@ struct UpdateWorkspace {
 size_t update_workspace_bytes(int64_t B, int64_t N, int64_t K);
 UpdateWorkspace carve_update_workspace(void* ws, int64_t B, int64_t N, int64_t K);
 
+// counts += histogram of the labels of ids that lie in [0,K).
 int launch_histogram(const int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K,
                      cudaStream_t stream);
+// offsets = exclusive scan of counts (which must be the histogram of ids), then
+// perm/ids_sorted. all_valid: every label lies in [0,K), so every sorted
+// position is written; otherwise unwritten positions read as label -1.
 int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
-                         int64_t B, int64_t N, int64_t K, cudaStream_t stream);
+                         int64_t B, int64_t N, int64_t K, bool all_valid, cudaStream_t stream);
 // sums[b, ids_sorted[i], :] += x[b, perm ? perm[i] : i, :] over sorted runs.
 // counts (nullable) += run lengths. sums/counts must be initialised by the caller.
 int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids_sorted,

@@ -7,18 +7,24 @@
 // Here:
 //   * the permutation comes from a counting sort on labels in [0, K):
 //     histogram (warp-aggregated atomics; fused into the assignment kernel on
-//     the Lloyd path) -> exclusive scan per batch row -> scatter of row indices
-//     (warp-aggregated cursors);
-//   * the accumulator walks sorted positions with one warp per range of 64
-//     positions: run boundaries come from a warp ballot, rows are gathered with
-//     16-byte vector loads (a D=128 fp16 row is 16 lanes x 16 B), partial sums
-//     live in registers and each run piece is flushed with 16-byte vector
-//     atomics (red.global.add.v4.f32). No sorted copy of x is written.
+//     the Lloyd path) -> exclusive scan per batch row -> scatter. The scatter
+//     ranks rows inside a chunk of 512-4096 rows with shared-memory atomics and
+//     claims each cluster's slots with one global atomic per (chunk, cluster),
+//     so a heavily populated cluster costs one global atomic per chunk, not per
+//     row;
+//   * the accumulator gives each warp 64 sorted positions and splits them into
+//     32/L contiguous row streams, L = lanes per row (a D=128 fp16 row is 16
+//     lanes x 16 B). Each stream keeps P rows in flight (16-byte non-allocating
+//     loads), accumulates in registers and flushes every run with 16-byte
+//     vector atomics (red.global.add.v4.f32). No sorted copy of x is written.
 // The same accumulator serves the reference's _C.centroid_update_sorted and
 // _C.centroid_update_sorted_indexed entry points (perm == nullptr for the
 // former).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <algorithm>
+#include <type_traits>
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
@@ -58,54 +64,140 @@ __global__ void histogram_kernel(const int32_t* __restrict__ ids, int32_t* __res
   }
 }
 
-// Exclusive scan of counts[b, 0..K) into offsets and cursor; one CTA per b.
-__global__ void __launch_bounds__(1024) scan_kernel(const int32_t* __restrict__ counts,
-                                                    int32_t* __restrict__ offsets,
-                                                    int32_t* __restrict__ cursor, int K) {
-  __shared__ int warp_tot[32];
-  const int b = blockIdx.x;
-  const int t = threadIdx.x;
-  const int lane = t & 31, w = t >> 5;
-  const int32_t* cnt = counts + static_cast<size_t>(b) * K;
-  const int per = (K + blockDim.x - 1) / blockDim.x;
-  const int beg = min(K, t * per), end = min(K, beg + per);
-  int local = 0;
-  for (int i = beg; i < end; ++i) local += cnt[i];
-  // inclusive warp scan
-  int v = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
-    if (lane >= o) v += u;
-  }
-  if (lane == 31) warp_tot[w] = v;
+// Exclusive scan of counts[b, 0..K) into offsets[b, 0..K) and cursor[b, 0..K);
+// one CTA of kScanThreads per b, V consecutive counts per thread per tile
+// (V = 4 with 16-byte loads and stores when K % 4 == 0).
+constexpr int kScanThreads = 1024;
+
+template <int V>
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(const int32_t* __restrict__ counts,
+                                                            int32_t* __restrict__ offsets,
+                                                            int32_t* __restrict__ cursor, int K) {
+  __shared__ int warp_tot[kScanThreads / 32];
+  __shared__ int carry_s;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int32_t* cnt = counts + static_cast<size_t>(blockIdx.x) * K;
+  int32_t* off = offsets + static_cast<size_t>(blockIdx.x) * K;
+  int32_t* cur = cursor + static_cast<size_t>(blockIdx.x) * K;
+  if (t == 0) carry_s = 0;
   __syncthreads();
-  if (w == 0) {
-    const int nw = blockDim.x >> 5;
-    int s = lane < nw ? warp_tot[lane] : 0;
+  for (int t0 = 0; t0 < K; t0 += kScanThreads * V) {
+    const int i0 = t0 + t * V;
+    int c[V];
+    if constexpr (V == 4) {
+      if (i0 < K) {
+        const int4 q = *reinterpret_cast<const int4*>(cnt + i0);
+        c[0] = q.x; c[1] = q.y; c[2] = q.z; c[3] = q.w;
+      } else {
+        c[0] = c[1] = c[2] = c[3] = 0;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e) c[e] = (i0 + e < K) ? cnt[i0 + e] : 0;
+    }
+    int local = 0;
+#pragma unroll
+    for (int e = 0; e < V; ++e) local += c[e];
+    int v = local;  // inclusive warp scan of the per-thread sums
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xFFFFFFFFu, s, o);
-      if (lane >= o) s += u;
+      const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
+      if (lane >= o) v += u;
     }
-    if (lane < nw) warp_tot[lane] = s;  // inclusive over warps
-  }
-  __syncthreads();
-  int run = v - local + (w > 0 ? warp_tot[w - 1] : 0);
-  int32_t* off = offsets + static_cast<size_t>(b) * K;
-  int32_t* cur = cursor + static_cast<size_t>(b) * K;
-  for (int i = beg; i < end; ++i) {
-    off[i] = run;
-    cur[i] = run;
-    run += cnt[i];
+    if (lane == 31) warp_tot[w] = v;
+    __syncthreads();
+    if (w == 0) {
+      int s = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, s, o);
+        if (lane >= o) s += u;
+      }
+      warp_tot[lane] = s;  // inclusive over warps
+    }
+    __syncthreads();
+    const int carry = carry_s;
+    int run = carry + v - local + (w > 0 ? warp_tot[w - 1] : 0);
+    int o[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      o[e] = run;
+      run += c[e];
+    }
+    if constexpr (V == 4) {
+      if (i0 < K) {
+        *reinterpret_cast<int4*>(off + i0) = make_int4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<int4*>(cur + i0) = make_int4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e)
+        if (i0 + e < K) off[i0 + e] = cur[i0 + e] = o[e];
+    }
+    __syncthreads();  // everyone has read carry_s and warp_tot
+    if (t == kScanThreads - 1) carry_s = run;
+    __syncthreads();
   }
 }
 
-// perm[b, pos] = n and ids_sorted[b, pos] = id, pos = offsets[b,id] + rank.
-// Rank within a cluster follows atomic order (not n order).
-__global__ void scatter_kernel(const int32_t* __restrict__ ids, int32_t* __restrict__ cursor,
-                               int32_t* __restrict__ perm, int32_t* __restrict__ ids_sorted,
-                               int64_t total, int64_t N, int K) {
+// Chunked scatter (K <= kLocalMaxK): the CTA ranks its rows per cluster with
+// shared-memory atomics, claims slots [base, base + local count) of each
+// cluster it holds with one global atomic on cursor, then writes
+// perm[b, base + local rank] = n and ids_sorted likewise. Within a cluster the
+// order follows the atomics (chunks in claim order, rows in rank order).
+constexpr int kSortThreads = 512;
+constexpr int kLocalMaxK = 16384;  // 64 KB of shared-memory counters
+
+template <int RPT>
+__global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
+    const int32_t* __restrict__ ids, int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
+    int32_t* __restrict__ ids_sorted, int N, int K, int chunks_per_batch) {
+  extern __shared__ int cnt[];  // K counters, then reused for the K slot bases
+  const int t = threadIdx.x;
+  const int b = blockIdx.x / chunks_per_batch;
+  const int r0 = (blockIdx.x - b * chunks_per_batch) * (kSortThreads * RPT);
+  const size_t rb = static_cast<size_t>(b) * N;
+  for (int k = t; k < K; k += kSortThreads) cnt[k] = 0;
+  __syncthreads();
+  int id[RPT], lr[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int n = r0 + i * kSortThreads + t;
+    id[i] = n < N ? ids[rb + n] : -1;
+    if (id[i] >= K) id[i] = -1;
+    lr[i] = id[i] >= 0 ? atomicAdd(&cnt[id[i]], 1) : 0;
+  }
+  __syncthreads();
+  int32_t* cur = cursor + static_cast<size_t>(b) * K;
+  for (int k0 = 0; k0 < K; k0 += kSortThreads * 8) {
+    int c[8], base[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = k0 + j * kSortThreads + t;
+      c[j] = k < K ? cnt[k] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      base[j] = c[j] > 0 ? atomicAdd(cur + k0 + j * kSortThreads + t, c[j]) : 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (c[j] > 0) cnt[k0 + j * kSortThreads + t] = base[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    if (id[i] < 0) continue;
+    const int pos = cnt[id[i]] + lr[i];
+    perm[rb + pos] = r0 + i * kSortThreads + t;
+    ids_sorted[rb + pos] = id[i];
+  }
+}
+
+// Scatter for any K: warp-aggregated atomics on the cursors.
+__global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
+                                      int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
+                                      int32_t* __restrict__ ids_sorted, int64_t total, int64_t N,
+                                      int K) {
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
@@ -142,6 +234,151 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
                "f"(c), "f"(d)
                : "memory");
+}
+
+// 16-byte load that does not allocate in L1 (each x row is read once here).
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint4& u) {
+  if constexpr (sizeof(T) == 4) {
+    acc[0] += __uint_as_float(u.x);
+    acc[1] += __uint_as_float(u.y);
+    acc[2] += __uint_as_float(u.z);
+    acc[3] += __uint_as_float(u.w);
+  } else {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f;
+      if constexpr (std::is_same<T, __half>::value)
+        f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+      acc[2 * k] += f.x;
+      acc[2 * k + 1] += f.y;
+    }
+  }
+}
+
+// Gather-accumulate over sorted positions. Each warp owns a span of
+// consecutive positions of one batch row (a multiple of 64, about equal spans
+// for all resident warps) and walks it in segments of 64 positions. A segment
+// is split into 32/L row streams of R = 2L consecutive positions; lane i of
+// stream g holds 16-byte vector i of the stream's current row. The labels and
+// source rows of a segment sit in two registers per lane (position
+// g*R + h*L + i in register h of lane g*L + i), so each step needs one shuffle
+// per value; the next segment's are loaded while the current one is walked.
+// Every stream keeps P row loads in flight, across segment boundaries. Rows of
+// one label are summed in registers (a stream's positions are sorted, so its
+// runs are contiguous even across segments) and flushed with vector atomics
+// when the label changes. Labels outside [0,K), including the -1 of unwritten
+// positions, load nothing and are never flushed.
+template <typename T, int L, int P>
+__global__ void __launch_bounds__(256) gather_accumulate_kernel(
+    const T* __restrict__ x, const int32_t* __restrict__ perm,
+    const int32_t* __restrict__ ids_sorted, float* __restrict__ sums,
+    int32_t* __restrict__ counts, int N, int K, int spans_per_batch, int span_len,
+    int64_t total_spans) {
+  constexpr int kVec = 16 / sizeof(T);
+  constexpr int R = 2 * L;  // positions per stream per 64-position segment
+  static_assert(32 % L == 0 && R % P == 0, "stream layout");
+  const int lane = threadIdx.x & 31;
+  const int g = lane / L;
+  const int i = lane % L;
+  const int D = L * kVec;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t sp = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+       sp < total_spans; sp += warps) {
+    const int b = static_cast<int>(sp / spans_per_batch);
+    const int sp0 = static_cast<int>(sp - static_cast<int64_t>(b) * spans_per_batch) * span_len;
+    const int sp1 = min(sp0 + span_len, N);
+    if (sp0 >= sp1) continue;
+    const int nseg = (sp1 - sp0 + kRange - 1) / kRange;
+    const size_t rb = static_cast<size_t>(b) * N;
+    const T* xb = x + rb * D;
+    auto load_meta = [&](int base, int (&lab)[2], int (&src)[2]) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q = base + g * R + h * L + i;
+        int l = q < sp1 ? ids_sorted[rb + q] : -1;
+        if (l >= K) l = -1;
+        lab[h] = l;
+        src[h] = l >= 0 ? (perm ? perm[rb + q] : q) : 0;
+      }
+    };
+    // Value of position g*R + j of the current segment (j known at compile time).
+    auto meta_at = [&](const int (&a)[2], int j) {
+      return __shfl_sync(0xFFFFFFFFu, a[j / L], g * L + (j % L));
+    };
+    auto load_row = [&](int src) {
+      return ld_stream_v4(xb + static_cast<size_t>(src) * D + i * kVec);
+    };
+    int lab[2], src[2], labn[2], srcn[2];
+    load_meta(sp0, lab, src);
+    int ring[P];  // labels of the rows in flight
+    uint4 buf[P];
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      ring[j] = meta_at(lab, j);
+      const int sr = meta_at(src, j);
+      if (ring[j] >= 0) buf[j] = load_row(sr);
+    }
+    float acc[kVec];
+#pragma unroll
+    for (int e = 0; e < kVec; ++e) acc[e] = 0.f;
+    int cur = -1, len = 0;
+    auto flush = [&]() {
+      if (cur >= 0) {
+        float* dst = sums + (static_cast<size_t>(b) * K + cur) * D + i * kVec;
+#pragma unroll
+        for (int e = 0; e < kVec; e += 4)
+          red_add_v4(dst + e, acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+        if (counts != nullptr && i == 0)
+          atomicAdd(counts + static_cast<size_t>(b) * K + cur, len);
+      }
+    };
+    for (int seg = 0; seg < nseg; ++seg) {
+      if (seg + 1 < nseg) {
+        load_meta(sp0 + (seg + 1) * kRange, labn, srcn);
+      } else {
+        labn[0] = labn[1] = -1;
+        srcn[0] = srcn[1] = 0;
+      }
+#pragma unroll
+      for (int j = 0; j < R; ++j) {
+        const int l = ring[j % P];
+        const int jn = j + P;  // the row whose load goes out at this step
+        const int ln = jn < R ? meta_at(lab, jn) : meta_at(labn, jn - R);
+        const int sn = jn < R ? meta_at(src, jn) : meta_at(srcn, jn - R);
+        if (l != cur) {
+          flush();
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) acc[e] = 0.f;
+          cur = l;
+          len = 0;
+        }
+        if (l >= 0) {
+          add_vec<T>(acc, buf[j % P]);
+          ++len;
+        }
+        ring[j % P] = ln;
+        if (ln >= 0) buf[j % P] = load_row(sn);
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        lab[h] = labn[h];
+        src[h] = srcn[h];
+      }
+    }
+    flush();
+  }
 }
 
 // Finds the end of the run of `id` starting at `pos` inside [pos, lim).
@@ -302,6 +539,42 @@ int grid_for(int64_t items, int per_block) {
   return static_cast<int>(g);
 }
 
+// Resident blocks of `kern` on this device (block size 256), for persistent grids.
+template <typename K>
+int resident_blocks(K kern) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return per_sm * sm_count_or_default();
+}
+
+template <typename T, int L>
+int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, float* sums,
+                  int32_t* counts, int64_t B, int64_t N, int64_t K, cudaStream_t stream) {
+  constexpr int R = 2 * L;
+  constexpr int P = R < 8 ? R : 8;
+  auto kern = gather_accumulate_kernel<T, L, P>;
+  static int cap = 0;  // resident blocks; the same on every device of one model
+  if (cap == 0) cap = resident_blocks(kern);
+  // About one span per resident warp, spans a multiple of 64 positions.
+  const int64_t warps = static_cast<int64_t>(cap) * 8;
+  int64_t spans_per_batch = std::max<int64_t>(1, (warps + B - 1) / B);
+  int64_t span_len = (N + spans_per_batch - 1) / spans_per_batch;
+  span_len = (span_len + kRange - 1) / kRange * kRange;
+  spans_per_batch = (N + span_len - 1) / span_len;
+  const int64_t total = spans_per_batch * B;
+  const int64_t blocks = std::min<int64_t>((total + 7) / 8, cap);
+  kern<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      x, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
+      static_cast<int>(spans_per_batch), static_cast<int>(span_len), total);
+  FKC_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
+  return FKC_OK;
+}
+
 template <typename T>
 int run_accumulate_typed(const void* x, const int32_t* perm, const int32_t* ids_sorted,
                          float* sums, int32_t* counts, int64_t B, int64_t N, int64_t K,
@@ -314,15 +587,26 @@ int run_accumulate_typed(const void* x, const int32_t* perm, const int32_t* ids_
   const bool vec_ok = row_bytes % 16 == 0 && row_bytes <= 512 &&
                       reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
                       reinterpret_cast<uintptr_t>(sums) % 16 == 0 && (D % 4 == 0);
+  const T* xt = static_cast<const T*>(x);
   if (vec_ok) {
     const int L = static_cast<int>(row_bytes / 16);
+    switch (L) {
+      case 1: return launch_gather<T, 1>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      case 2: return launch_gather<T, 2>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      case 4: return launch_gather<T, 4>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      case 8: return launch_gather<T, 8>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      case 16: return launch_gather<T, 16>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      case 32: return launch_gather<T, 32>(xt, perm, ids_sorted, sums, counts, B, N, K, stream);
+      default:
+        break;
+    }
     run_accumulate_vec_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const T*>(x), perm, ids_sorted, sums, counts, static_cast<int>(N),
-        static_cast<int>(K), static_cast<int>(D), L, static_cast<int>(ranges_per_batch), total);
+        xt, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
+        static_cast<int>(D), L, static_cast<int>(ranges_per_batch), total);
   } else {
     run_accumulate_scalar_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const T*>(x), perm, ids_sorted, sums, counts, static_cast<int>(N),
-        static_cast<int>(K), static_cast<int>(D), static_cast<int>(ranges_per_batch), total);
+        xt, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
+        static_cast<int>(D), static_cast<int>(ranges_per_batch), total);
   }
   FKC_CUDA_TRY(cudaGetLastError());
   count_launches(1);
@@ -359,19 +643,56 @@ int launch_histogram(const int32_t* ids, int32_t* counts, int64_t B, int64_t N, 
   return FKC_OK;
 }
 
-int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
-                         int64_t B, int64_t N, int64_t K, cudaStream_t stream) {
-  FKC_REQUIRE(B <= 2147483647ll, "update: B too large");
-  scan_kernel<<<static_cast<unsigned>(B), 1024, 0, stream>>>(counts, w.offsets, w.cursor,
-                                                             static_cast<int>(K));
+namespace {
+
+template <int RPT>
+int launch_scatter_chunk(const int32_t* ids, const UpdateWorkspace& w, int64_t B, int64_t N,
+                         int64_t K, cudaStream_t stream) {
+  auto kern = scatter_chunk_kernel<RPT>;
+  const int smem = static_cast<int>(K) * 4;
+  if (smem > 48 * 1024)
+    FKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t chunks = (N + kSortThreads * RPT - 1) / (kSortThreads * RPT);
+  FKC_REQUIRE(chunks * B < (1ll << 31), "update: too many row chunks");
+  kern<<<static_cast<unsigned>(chunks * B), kSortThreads, smem, stream>>>(
+      ids, w.cursor, w.perm, w.ids_sorted, static_cast<int>(N), static_cast<int>(K),
+      static_cast<int>(chunks));
   FKC_CUDA_TRY(cudaGetLastError());
   count_launches(1);
-  // Positions not filled by the scatter (labels outside [0,K)) read as -1 and
-  // are skipped by the accumulator.
-  FKC_CUDA_TRY(cudaMemsetAsync(w.ids_sorted, 0xFF, static_cast<size_t>(B * N) * 4, stream));
+  return FKC_OK;
+}
+
+}  // namespace
+
+int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
+                         int64_t B, int64_t N, int64_t K, bool all_valid, cudaStream_t stream) {
+  FKC_REQUIRE(B <= 2147483647ll && N <= 2147483647ll && K <= 2147483647ll,
+              "update: sizes out of range");
+  if (K % 4 == 0)
+    scan_kernel<4><<<static_cast<unsigned>(B), kScanThreads, 0, stream>>>(
+        counts, w.offsets, w.cursor, static_cast<int>(K));
+  else
+    scan_kernel<1><<<static_cast<unsigned>(B), kScanThreads, 0, stream>>>(
+        counts, w.offsets, w.cursor, static_cast<int>(K));
+  FKC_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
+  // With labels outside [0,K) some sorted positions stay unwritten: they must
+  // read as label -1, which the accumulator skips.
+  if (!all_valid)
+    FKC_CUDA_TRY(cudaMemsetAsync(w.ids_sorted, 0xFF, static_cast<size_t>(B * N) * 4, stream));
+  if (K <= kLocalMaxK) {
+    // Rows per chunk: the largest of 4096/2048/1024/512 that still gives about
+    // two chunks per SM.
+    const int64_t rows = B * N;
+    const int64_t want = 2ll * sm_count_or_default();
+    if (rows >= want * kSortThreads * 8) return launch_scatter_chunk<8>(ids, w, B, N, K, stream);
+    if (rows >= want * kSortThreads * 4) return launch_scatter_chunk<4>(ids, w, B, N, K, stream);
+    if (rows >= want * kSortThreads * 2) return launch_scatter_chunk<2>(ids, w, B, N, K, stream);
+    return launch_scatter_chunk<1>(ids, w, B, N, K, stream);
+  }
   const int64_t total = B * N;
-  scatter_kernel<<<grid_for(total, 256), 256, 0, stream>>>(ids, w.cursor, w.perm, w.ids_sorted,
-                                                           total, N, static_cast<int>(K));
+  scatter_atomic_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
+      ids, w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K));
   FKC_CUDA_TRY(cudaGetLastError());
   count_launches(1);
   return FKC_OK;
