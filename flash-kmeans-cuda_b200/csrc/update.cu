@@ -188,6 +188,7 @@ __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
   for (int i = 0; i < RPT; ++i) {
     if (id[i] < 0) continue;
     const int pos = cnt[id[i]] + lr[i];
+    if (pos >= N) continue;  // counts inconsistent with ids: drop rather than overrun
     perm[rb + pos] = r0 + i * kSortThreads + t;
     ids_sorted[rb + pos] = id[i];
   }
@@ -223,9 +224,11 @@ __global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
       if (lane == leader) pos0 = atomicAdd(cursor + key, __popc(peers));
       pos0 = __shfl_sync(peers, pos0, leader);
       const int pos = pos0 + __popc(peers & lanemask_lt());
-      const int64_t dst = b * N + pos;
-      perm[dst] = static_cast<int32_t>(i - b * N);
-      ids_sorted[dst] = id;
+      if (pos < N) {  // counts inconsistent with ids: drop rather than overrun
+        const int64_t dst = b * N + pos;
+        perm[dst] = static_cast<int32_t>(i - b * N);
+        ids_sorted[dst] = id;
+      }
     }
   }
 }
@@ -309,8 +312,13 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
         const int q = base + g * R + h * L + i;
         int l = q < sp1 ? ids_sorted[rb + q] : -1;
         if (l >= K) l = -1;
+        int sr = l >= 0 ? (perm ? perm[rb + q] : q) : 0;
+        if (sr < 0 || sr >= N) {  // a caller's bad row index reads nothing
+          l = -1;
+          sr = 0;
+        }
         lab[h] = l;
-        src[h] = l >= 0 ? (perm ? perm[rb + q] : q) : 0;
+        src[h] = sr;
       }
     };
     // Value of position g*R + j of the current segment (j known at compile time).
