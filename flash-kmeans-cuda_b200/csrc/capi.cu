@@ -59,7 +59,10 @@ int set_error(int status, const char* fmt, ...) {
 
 void clear_error() { g_last_error[0] = '\0'; }
 
-void count_launches(int n) { g_launches.fetch_add(static_cast<uint64_t>(n)); }
+void count_launches(int n) {
+  if (count_captured_launch(n)) return;  // recorded into a graph, counted per replay
+  g_launches.fetch_add(static_cast<uint64_t>(n));
+}
 
 int current_device_info(const DeviceInfo** out) {
   int dev = -1;
@@ -171,11 +174,14 @@ struct LloydWs {
   uint8_t* cext = nullptr;  // (B,K,16) bf16, tensor-core path
   float* c_sq = nullptr;    // (B,K) fp32
   UpdateWorkspace upd{};
+  LoopCtl* ctl = nullptr;   // whole-loop graph control block
 };
+
+constexpr size_t kCtlBytes = 256;
 
 size_t lloyd_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   return assign_ws_bytes(B, N, K, D, dtype) + align_up(static_cast<size_t>(B * K) * 4, 256) +
-         update_workspace_bytes(B, N, K);
+         update_workspace_bytes(B, N, K) + kCtlBytes;
 }
 
 int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
@@ -196,6 +202,8 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
   out->c_sq = reinterpret_cast<float*>(p);
   p += align_up(static_cast<size_t>(B * K) * 4, 256);
   out->upd = carve_update_workspace(p, B, N, K);
+  p += update_workspace_bytes(B, N, K);
+  out->ctl = reinterpret_cast<LoopCtl*>(p);
   return FKC_OK;
 }
 
@@ -429,6 +437,50 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
                           workspace_bytes, stream));
   return fkc_lloyd_finalize(sums, counts, old_c, new_c, shift_out, B, N, K, D, dtype, workspace,
                             workspace_bytes, stream);
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_run(const void* x, void* centroids, int32_t* ids, float* sums,
+                                  int32_t* counts, float* shift, int32_t* n_iters, int max_iters,
+                                  float tol, int64_t B, int64_t N, int64_t K, int64_t D,
+                                  int dtype, void* workspace, size_t workspace_bytes,
+                                  fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, N, K, D, dtype));
+  FKC_REQUIRE(x && centroids && ids && sums && counts && shift, "null argument");
+  FKC_REQUIRE(max_iters >= 0, "max_iters must be >= 0 (got %d)", max_iters);
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  const cudaStream_t st = as_stream(stream);
+  // Centroid terms of the initial centroids (later iterations: finalize).
+  FKC_TRY(launch_cnorm_ext(centroids, nullptr, w.cext, w.c_sq, B, K, D, dtype, st));
+  if (max_iters == 0) {
+    if (n_iters != nullptr) FKC_CUDA_TRY(cudaMemsetAsync(n_iters, 0, sizeof(int32_t), st));
+    return FKC_OK;
+  }
+  int dev = 0;
+  FKC_CUDA_TRY(cudaGetDevice(&dev));
+  LloydGraphKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.device = dev;
+  key.dtype = dtype;
+  key.x = x;
+  key.centroids = centroids;
+  key.ids = ids;
+  key.sums = sums;
+  key.counts = counts;
+  key.shift = shift;
+  key.workspace = workspace;
+  key.B = B;
+  key.N = N;
+  key.K = K;
+  key.D = D;
+  // One in-place iteration: finalize reads each old centroid element before
+  // writing the new one, and the next assign reads the updated centroids.
+  const LoopBody body = [&](cudaStream_t cs) -> int {
+    return fkc_lloyd_iter(x, centroids, centroids, ids, sums, counts, shift, B, N, K, D, dtype,
+                          workspace, workspace_bytes, reinterpret_cast<fkc_stream_t>(cs));
+  };
+  return run_lloyd_graph(key, body, w.ctl, shift, max_iters, tol, n_iters, st);
 }
 
 }  // extern "C"

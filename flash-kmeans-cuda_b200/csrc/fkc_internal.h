@@ -8,6 +8,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <cstdio>
 #include <string>
 
@@ -116,6 +117,38 @@ int launch_counting_sort(const int32_t* ids, const int32_t* counts, const Update
 int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids_sorted,
                           float* sums, int32_t* counts, int64_t B, int64_t N, int64_t K,
                           int64_t D, int dtype, cudaStream_t stream);
+
+// Whole-loop CUDA graph (lloyd_graph.cu).
+struct LoopCtl {
+  int32_t iter;       // iterations completed in the current launch
+  int32_t max_iters;
+  float tol;          // stop when the shift falls below tol (tol > 0)
+  int32_t n_iters;    // iterations run (read after the launch)
+};
+// Identifies the buffers and shape a cached graph was captured for. Built
+// with memset(0) so that padding compares equal.
+struct LloydGraphKey {
+  int device;
+  int dtype;
+  const void* x;
+  void* centroids;
+  int32_t* ids;
+  float* sums;
+  int32_t* counts;
+  float* shift;
+  void* workspace;
+  int64_t B, N, K, D;
+};
+using LoopBody = std::function<int(cudaStream_t)>;
+// Launches (building and caching on first use) WHILE { body; control } with
+// at most max_iters iterations; writes the iterations run to n_iters_out
+// (device, nullable). ctl: device control block; shift: the body's shift.
+int run_lloyd_graph(const LloydGraphKey& key, const LoopBody& body, LoopCtl* ctl,
+                    const float* shift, int max_iters, float tol, int32_t* n_iters_out,
+                    cudaStream_t stream);
+// True (and the launches recorded for the graph) while this thread captures.
+bool count_captured_launch(int n);
+uint64_t capture_launch_count();
 
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,

@@ -7,8 +7,11 @@ kernels all run on the current stream:
   assign (tcgen05, labels + fused label histogram) -> scan -> scatter
   -> gather-accumulate -> finalize (+ next ||c||^2 terms, + shift)
 
-The host synchronises only when the shift is needed (``tol > 0`` or
-``verbose``), exactly when the reference calls ``.item()``.
+``batch_kmeans_Euclid`` runs the whole loop as one CUDA graph launch
+(``fkc_lloyd_run``: a device-side while loop that also applies ``tol``), and
+synchronises once, at the end, to read the number of iterations. With
+``verbose=True`` it steps iteration by iteration instead, reading the shift
+after each one as the reference does.
 """
 
 from __future__ import annotations
@@ -84,6 +87,20 @@ class LloydState:
                                               self.shift.data_ptr() if want_shift else None,
                                               *self._dims()), "fkc_lloyd_finalize")
 
+    def run(self, c: torch.Tensor, max_iters: int, tol: float) -> torch.Tensor:
+        """The whole loop on the device, centroids ``c`` updated in place.
+
+        Returns the number of iterations run as a (1,) int32 device tensor.
+        """
+        self._check_c(c)
+        n = torch.zeros((1,), dtype=torch.int32, device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.fkc_lloyd_run(self.x.data_ptr(), c.data_ptr(), self.ids.data_ptr(),
+                                         self.sums.data_ptr(), self.counts.data_ptr(),
+                                         self.shift.data_ptr(), n.data_ptr(), int(max_iters),
+                                         float(tol), *self._dims()), "fkc_lloyd_run")
+        return n
+
     def step(self, old: torch.Tensor, new: torch.Tensor, want_shift: bool) -> None:
         """One full Lloyd iteration: ids/sums/counts from ``old``, centroids into ``new``."""
         with torch.cuda.device(self.device):
@@ -143,9 +160,12 @@ def batch_kmeans_Euclid(
         centroids = init_centroids.contiguous().clone()
     centroids = centroids.view(B, n_clusters, D)
 
-    need_shift = tol > 0 or verbose
     state = LloydState(x, n_clusters)
     state._check_c(centroids)
+    if not verbose:
+        n = state.run(centroids, max_iters, tol)
+        return state.ids, centroids, int(n.item())
+    need_shift = True
     cur, nxt = centroids, torch.empty_like(centroids)
     state.set_centroids(cur)
     n_iters_run = 0

@@ -212,6 +212,29 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
                                    int64_t N, int64_t K, int64_t D, int dtype, void* workspace,
                                    size_t workspace_bytes, fkc_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * The whole Lloyd loop (batch_kmeans_Euclid without init, kmeans.py:162-195)
+ * as ONE CUDA graph launch: a device-side WHILE loop over in-place iterations
+ * (assign -> update -> finalize) that stops after max_iters iterations or,
+ * when tol > 0, after the first iteration whose shift is below tol. No host
+ * synchronisation inside the loop.
+ *   centroids (B,K,D): initial centroids in, final centroids out (in place).
+ *   ids: labels of the last assignment (against the centroids entering the
+ *   last iteration); sums/counts: of the last iteration; shift (1) fp32
+ *   device: shift of the last iteration; n_iters (1) int32 device, nullable:
+ *   iterations run. Call fkc_lloyd_prepare(x) first (workspace of
+ *   fkc_lloyd_workspace_size).
+ * The first call for a set of buffers and shape captures and instantiates the
+ * graph (host cost about a millisecond); later calls with the same pointers
+ * replay it. Do not call it while the stream is being captured.
+ * Replaces: the Python loop of batch_kmeans_Euclid (kmeans.py:162-195).
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT int fkc_lloyd_run(const void* x, void* centroids, int32_t* ids, float* sums,
+                                  int32_t* counts, float* shift, int32_t* n_iters, int max_iters,
+                                  float tol, int64_t B, int64_t N, int64_t K, int64_t D,
+                                  int dtype, void* workspace, size_t workspace_bytes,
+                                  fkc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

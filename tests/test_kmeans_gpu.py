@@ -151,3 +151,64 @@ def test_kmeans_rejects_bad_input(cuda_device):
     with pytest.raises(RuntimeError, match="share dtype"):
         batch_kmeans_Euclid(torch.randn(1, 10, 16, device="cuda", dtype=torch.float16), 2,
                             init_centroids=torch.randn(1, 2, 16, device="cuda"))
+
+
+def _stepwise(x, init, max_iters, tol):
+    """Iteration-by-iteration loop (fkc_lloyd_iter per step, shift read each step)."""
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    st = LloydState(x, init.shape[1])
+    cur, nxt = init.clone(), torch.empty_like(init)
+    st.set_centroids(cur)
+    n = 0
+    for it in range(max_iters):
+        st.step(cur, nxt, True)
+        n = it + 1
+        if tol > 0 and st.shift.item() < tol:
+            cur = nxt
+            break
+        cur, nxt = nxt, cur
+    return st.ids.clone(), cur, n
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("tol", [0.0, 1e-3])
+def test_graph_loop_matches_stepwise(cuda_device, dtype, tol):
+    """The whole-loop graph (device-side while + tol) runs the same iterations as
+    the host-driven loop: same iteration count, labels >= 99.9% equal and
+    centroids within 1e-3 (sums are atomic, so the last bits may differ)."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+
+    x = mixture(1, 16384, 64, 32, seed=21, dtype=dtype).cuda()
+    init = subset_init(x.cpu(), 32, seed=22).cuda()
+    ids_g, c_g, n_g = batch_kmeans_Euclid(x, 32, max_iters=30, tol=tol, init_centroids=init)
+    ids_s, c_s, n_s = _stepwise(x, init, 30, tol)
+    torch.cuda.synchronize()
+    assert n_g == n_s
+    assert (ids_g == ids_s).float().mean().item() >= 0.999
+    _close_centroids(to_np(c_g.cpu()), to_np(c_s.cpu()), dtype)
+
+
+def test_graph_loop_replay_and_edges(cuda_device):
+    """Second call on the same buffers replays the cached graph; max_iters=0 and
+    tol larger than any shift are handled on the device."""
+    from flash_kmeans_cuda import _lib
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    x = mixture(2, 8192, 128, 64, seed=31).cuda()
+    init = subset_init(x.cpu(), 64, seed=32).cuda()
+    st = LloydState(x, 64)
+    results = []
+    for _ in range(2):
+        c = init.clone()
+        n = st.run(c, 6, 0.0)
+        torch.cuda.synchronize()
+        results.append((st.ids.clone(), c, int(n.item())))
+    assert results[0][2] == results[1][2] == 6
+    assert torch.equal(results[0][0], results[1][0])
+    _close_centroids(to_np(results[0][1].cpu()), to_np(results[1][1].cpu()), "float16")
+    c = init.clone()
+    assert int(st.run(c, 0, 0.0).item()) == 0 and torch.equal(c, init)
+    c = init.clone()
+    assert int(st.run(c, 50, 1e30).item()) == 1  # every shift is below tol: one iteration
+    _lib.device_status()
