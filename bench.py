@@ -327,7 +327,8 @@ def run_reference_arm(args, w: dict) -> None:
 def run_ours(args, w: dict) -> None:
     import flash_kmeans_cuda as fkc
     from flash_kmeans_cuda import _C, _lib
-    from flash_kmeans_cuda.distributed import batch_kmeans_Euclid_sharded, shard_bounds
+    from flash_kmeans_cuda.distributed import (allreduce_sums_counts,
+                                               batch_kmeans_Euclid_sharded, shard_bounds)
     from flash_kmeans_cuda.kmeans import LloydState
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -364,8 +365,7 @@ def run_ours(args, w: dict) -> None:
         a, b = bufs[i % 2], bufs[(i + 1) % 2]
         if w["shard"] == "N" and world > 1:
             st.local(a)
-            dist.all_reduce(st.sums)
-            dist.all_reduce(st.counts)
+            allreduce_sums_counts(st.sums, st.counts)
             st.finalize(a, b, False)
         else:
             st.step(a, b, False)

@@ -65,6 +65,20 @@ def _broadcast_init(x_local: torch.Tensor, n_clusters: int, group) -> torch.Tens
     return c
 
 
+def allreduce_sums_counts(sums: torch.Tensor, counts: torch.Tensor, group=None) -> None:
+    """Sum ``sums`` (fp32) and ``counts`` (int32) over the group; with NCCL as ONE
+    grouped collective (one NCCL group launch instead of two all-reduces).
+    Counts stay int32, exact for any point count below 2**31."""
+    if dist.get_backend(group) == "nccl":
+        with dist._coalescing_manager(group=group, device=sums.device, async_ops=True) as cm:
+            dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+            dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+        cm.wait()
+        return
+    dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+
+
 def batch_kmeans_Euclid_sharded(
     x_local: torch.Tensor,
     n_clusters: int,
@@ -123,8 +137,7 @@ def batch_kmeans_Euclid_sharded(
         if shard == "N":
             state.local(cur)
             if world > 1:
-                dist.all_reduce(state.sums, op=dist.ReduceOp.SUM, group=group)
-                dist.all_reduce(state.counts, op=dist.ReduceOp.SUM, group=group)
+                allreduce_sums_counts(state.sums, state.counts, group)
             state.finalize(cur, nxt, need_shift)
         else:
             state.step(cur, nxt, need_shift)
