@@ -66,15 +66,9 @@ def _broadcast_init(x_local: torch.Tensor, n_clusters: int, group) -> torch.Tens
 
 
 def allreduce_sums_counts(sums: torch.Tensor, counts: torch.Tensor, group=None) -> None:
-    """Sum ``sums`` (fp32) and ``counts`` (int32) over the group; with NCCL as ONE
-    grouped collective (one NCCL group launch instead of two all-reduces).
-    Counts stay int32, exact for any point count below 2**31."""
-    if dist.get_backend(group) == "nccl":
-        with dist._coalescing_manager(group=group, device=sums.device, async_ops=True) as cm:
-            dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
-            dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
-        cm.wait()
-        return
+    """Sum ``sums`` (fp32) and ``counts`` (int32) over the group (two all-reduces:
+    the collectives cannot be grouped across dtypes, and counts stay int32, exact
+    for any point count below 2**31)."""
     dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
     dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
 
