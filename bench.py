@@ -327,8 +327,9 @@ def run_reference_arm(args, w: dict) -> None:
 def run_ours(args, w: dict) -> None:
     import flash_kmeans_cuda as fkc
     from flash_kmeans_cuda import _C, _lib
-    from flash_kmeans_cuda.distributed import (allreduce_sums_counts,
-                                               batch_kmeans_Euclid_sharded, shard_bounds)
+    from flash_kmeans_cuda.distributed import (MultimemLloyd, allreduce_sums_counts,
+                                               batch_kmeans_Euclid_sharded, multimem_enabled,
+                                               shard_bounds)
     from flash_kmeans_cuda.kmeans import LloydState
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -355,15 +356,26 @@ def run_ours(args, w: dict) -> None:
     torch.cuda.empty_cache()
     Bl, Nl = x.shape[0], x.shape[1]
 
-    st = LloydState(x, K)
-    cur = init.clone()
-    nxt = torch.empty_like(cur)
-    st.set_centroids(cur)
-    bufs = [cur, nxt]
+    mm = None
+    if w["shard"] == "N" and world > 1 and multimem_enabled() and MultimemLloyd.available(x):
+        # sums/counts all-reduce fused into the finalize over NVLink multicast
+        n_max = max(b1 - b0 for b0, b1 in (shard_bounds(N, world, r) for r in range(world)))
+        mm = MultimemLloyd(x, K, n_max)
+        mm.set_centroids(init)
+        st = mm.state
+        bufs = [mm.centroids, mm.centroids]
+    else:
+        st = LloydState(x, K)
+        cur = init.clone()
+        nxt = torch.empty_like(cur)
+        st.set_centroids(cur)
+        bufs = [cur, nxt]
 
     def step(i):
         a, b = bufs[i % 2], bufs[(i + 1) % 2]
-        if w["shard"] == "N" and world > 1:
+        if mm is not None:
+            mm.step(i, False)
+        elif w["shard"] == "N" and world > 1:
             st.local(a)
             allreduce_sums_counts(st.sums, st.counts)
             st.finalize(a, b, False)
@@ -385,6 +397,8 @@ def run_ours(args, w: dict) -> None:
         barrier_sync(dev)
     launches = int(_lib.lib.fkc_kernel_launches() - launches0)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    if mm is not None:
+        mm.release()  # every rank past the last multicast kernel before phase timings
 
     # Per-phase timings on the resident data (assign / update / finalize).
     cur_c = bufs[(args.warmup + args.steps) % 2]   # centroids produced by the last step
@@ -476,7 +490,8 @@ def run_ours(args, w: dict) -> None:
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": DT_SHORT[w["dtype"]], "data": "synthetic",
             "config": {"workload": args.workload, "B": B, "N": N, "K": K, "D": D,
-                       "parallelism": f"dp{world}-shard{w['shard']}",
+                       "parallelism": (f"dp{world}-shard{w['shard']}"
+                                       + ("-multimem" if mm is not None else "")),
                        "l2": (f"x ({B * N * D * esz / 1e6:.0f} MB) > L2 (126 MB): no flush"
                               if B * N * D * esz > L2_BYTES else "x fits in L2")},
             "assign_tflops": tflops,

@@ -192,18 +192,24 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
                      ws_bytes, ws);
   FKC_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255u) == 0,
               "workspace must be 256-byte aligned");
+  // Parts that depend only on (B, K, D, dtype) come first, at the same offsets
+  // for every N: ranks holding different numbers of points share the layout
+  // of the centroid terms (fkc_lloyd_finalize_multimem writes them remotely).
   uint8_t* p = static_cast<uint8_t*>(ws);
-  if (tc_shape_ok(D, dtype)) {
-    out->aext = p;
-    p += align_up(static_cast<size_t>(B * N) * 32, 256);
+  const bool tc = tc_shape_ok(D, dtype);
+  if (tc) {
     out->cext = p;
     p += align_up(static_cast<size_t>(B * K) * 32, 256);
   }
   out->c_sq = reinterpret_cast<float*>(p);
   p += align_up(static_cast<size_t>(B * K) * 4, 256);
-  out->upd = carve_update_workspace(p, B, N, K);
-  p += update_workspace_bytes(B, N, K);
   out->ctl = reinterpret_cast<LoopCtl*>(p);
+  p += kCtlBytes;
+  if (tc) {
+    out->aext = p;
+    p += align_up(static_cast<size_t>(B * N) * 32, 256);
+  }
+  out->upd = carve_update_workspace(p, B, N, K);
   return FKC_OK;
 }
 
@@ -437,6 +443,30 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
                           workspace_bytes, stream));
   return fkc_lloyd_finalize(sums, counts, old_c, new_c, shift_out, B, N, K, D, dtype, workspace,
                             workspace_bytes, stream);
+}
+
+FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem(
+    const float* mc_sums, const int32_t* mc_counts, const void* centroids, void* mc_centroids,
+    void* mc_workspace, unsigned int* mc_shift, float* shift_clear, int64_t row_begin,
+    int64_t row_end, int64_t B, int64_t K, int64_t D, int dtype, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, 1, K, D, dtype));
+  FKC_REQUIRE(mc_sums && mc_counts && centroids && mc_centroids && mc_workspace,
+              "null argument");
+  FKC_REQUIRE(row_begin >= 0 && row_begin <= row_end && row_end <= B * K,
+              "rows [%lld, %lld) outside [0, B*K=%lld)", static_cast<long long>(row_begin),
+              static_cast<long long>(row_end), static_cast<long long>(B * K));
+  // The centroid terms sit at offsets that do not depend on N.
+  LloydWs w;
+  FKC_TRY(carve_lloyd(mc_workspace, lloyd_ws_bytes(B, 1, K, D, dtype), B, 1, K, D, dtype, &w));
+  if (row_begin == row_end) {
+    if (shift_clear != nullptr)
+      FKC_CUDA_TRY(cudaMemsetAsync(shift_clear, 0, sizeof(float), as_stream(stream)));
+    return FKC_OK;
+  }
+  return launch_finalize_multimem(mc_sums, mc_counts, centroids, mc_centroids, w.c_sq, w.cext,
+                                  mc_shift, shift_clear, row_begin, row_end, D, dtype,
+                                  as_stream(stream));
 }
 
 FKC_CAPI_EXPORT int fkc_lloyd_run(const void* x, void* centroids, int32_t* ids, float* sums,

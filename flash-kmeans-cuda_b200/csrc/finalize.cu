@@ -53,7 +53,165 @@ __global__ void __launch_bounds__(256) finalize_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Multi-GPU finalize over NVLink multicast. Every rank holds its own per-cluster
+// sums/counts in a symmetric buffer; a rank finalizes only the centroid rows
+// [row0, row1) of the flattened (B*K) rows: it reads the SUM over all ranks
+// with multimem.ld_reduce (the NVSwitch adds the copies), and writes each new
+// row, its ||c||^2 and its norm-slice row to every rank with multimem.st. The
+// shift is max-reduced with multimem.red.max on the bits of a non-negative
+// float. So the all-reduce of sums/counts and the replicated finalize become
+// one kernel whose NVLink traffic per rank is one slice of the sums in and the
+// new centroids out.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float4 mc_ld_reduce_v4(const float* mc) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mc_ld_reduce_u32(const int32_t* mc) {
+  uint32_t r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.u32 %0, [%1];"
+               : "=r"(r)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ void mc_st_v2(void* mc, uint32_t a, uint32_t b) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc),
+               "f"(__uint_as_float(a)), "f"(__uint_as_float(b))
+               : "memory");
+}
+
+__device__ __forceinline__ void mc_st_v4(void* mc, uint32_t a, uint32_t b, uint32_t c,
+                                         uint32_t d) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "f"(__uint_as_float(a)), "f"(__uint_as_float(b)), "f"(__uint_as_float(c)),
+               "f"(__uint_as_float(d))
+               : "memory");
+}
+
+__device__ __forceinline__ void mc_st_f32(void* mc, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void mc_red_max_u32(void* mc, uint32_t v) {
+  asm volatile("multimem.red.relaxed.sys.global.max.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(T a, T b) {
+  static_assert(sizeof(T) == 2, "16-bit element");
+  uint16_t ua, ub;
+  memcpy(&ua, &a, 2);
+  memcpy(&ub, &b, 2);
+  return static_cast<uint32_t>(ua) | (static_cast<uint32_t>(ub) << 16);
+}
+
+// D % 4 == 0: lane l owns elements [4l + 128i, 4l + 128i + 4) of the row.
+template <typename T>
+__global__ void __launch_bounds__(256) finalize_multimem_kernel(
+    const float* __restrict__ mc_sums, const int32_t* __restrict__ mc_counts,
+    const T* __restrict__ old_c, T* mc_new_c, float* mc_c_sq, uint8_t* mc_cext,
+    unsigned int* mc_shift, float* shift_clear, int64_t row0, int64_t row1, int D) {
+  const int lane = threadIdx.x & 31;
+  if (shift_clear != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *shift_clear = 0.f;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = row0 + static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) +
+                   (threadIdx.x >> 5);
+       r < row1; r += warps_total) {
+    int32_t cnt = 0;
+    if (lane == 0) cnt = static_cast<int32_t>(mc_ld_reduce_u32(mc_counts + r));
+    cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
+    const float fc = static_cast<float>(cnt);
+    float sq = 0.f, sh = 0.f;
+    for (int d = 4 * lane; d < D; d += 128) {
+      const float4 sv = mc_ld_reduce_v4(mc_sums + r * D + d);
+      const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+      T nv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const T ov = old_c[r * D + d + e];
+        nv[e] = cnt > 0 ? from_f32<T>(__fdiv_rn(s4[e], fc)) : ov;
+        const float nf = to_f32<T>(nv[e]);
+        const float df = nf - to_f32<T>(ov);
+        sq = fmaf(nf, nf, sq);
+        sh = fmaf(df, df, sh);
+      }
+      if constexpr (sizeof(T) == 4) {
+        mc_st_v4(mc_new_c + r * D + d, __float_as_uint(to_f32<T>(nv[0])),
+                 __float_as_uint(to_f32<T>(nv[1])), __float_as_uint(to_f32<T>(nv[2])),
+                 __float_as_uint(to_f32<T>(nv[3])));
+      } else {
+        mc_st_v2(mc_new_c + r * D + d, pack2<T>(nv[0], nv[1]), pack2<T>(nv[2], nv[3]));
+      }
+    }
+    sq = warp_sum(sq);
+    sh = warp_sum(sh);
+    if (lane == 0) {
+      if (mc_c_sq != nullptr) mc_st_f32(mc_c_sq + r, sq);
+      if (mc_cext != nullptr) {
+        alignas(16) uint8_t row[kNormExtBytes];
+        write_norm_ext(row, -0.5f * sq, false);
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(row);
+        mc_st_v4(mc_cext + r * kNormExtBytes, w[0], w[1], w[2], w[3]);
+        mc_st_v4(mc_cext + r * kNormExtBytes + 16, w[4], w[5], w[6], w[7]);
+      }
+      if (mc_shift != nullptr) mc_red_max_u32(mc_shift, __float_as_uint(sqrtf(sh)));
+    }
+  }
+  // The multicast stores and reductions are ordered before whatever follows
+  // this kernel on the stream (the cross-GPU barrier's release).
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 }  // namespace
+
+int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, const void* old_c,
+                             void* mc_new_c, float* mc_c_sq, void* mc_cext,
+                             unsigned int* mc_shift, float* shift_clear, int64_t row0,
+                             int64_t row1, int64_t D, int dtype, cudaStream_t stream) {
+  FKC_REQUIRE(D % 4 == 0, "finalize_multimem: D must be a multiple of 4 (got %lld)",
+              static_cast<long long>(D));
+  const int64_t rows = row1 - row0;
+  const DeviceInfo* di = nullptr;
+  FKC_TRY(current_device_info(&di));
+  int64_t grid = (rows + 7) / 8;
+  const int64_t cap = static_cast<int64_t>(di->sm_count) * 16;
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  uint8_t* ce = static_cast<uint8_t*>(mc_cext);
+  const int d = static_cast<int>(D);
+  switch (dtype) {
+    case FKC_DTYPE_F16:
+      finalize_multimem_kernel<__half><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+          mc_sums, mc_counts, static_cast<const __half*>(old_c), static_cast<__half*>(mc_new_c),
+          mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
+      break;
+    case FKC_DTYPE_BF16:
+      finalize_multimem_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+          mc_sums, mc_counts, static_cast<const __nv_bfloat16*>(old_c),
+          static_cast<__nv_bfloat16*>(mc_new_c), mc_c_sq, ce, mc_shift, shift_clear, row0, row1,
+          d);
+      break;
+    case FKC_DTYPE_F32:
+      finalize_multimem_kernel<float><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+          mc_sums, mc_counts, static_cast<const float*>(old_c), static_cast<float*>(mc_new_c),
+          mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
+      break;
+    default:
+      return set_error(FKC_EINVAL, "finalize_multimem: bad dtype %d", dtype);
+  }
+  FKC_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
+  return FKC_OK;
+}
 
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,

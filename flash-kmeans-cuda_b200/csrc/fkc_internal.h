@@ -150,6 +150,13 @@ int run_lloyd_graph(const LloydGraphKey& key, const LoopBody& body, LoopCtl* ctl
 bool count_captured_launch(int n);
 uint64_t capture_launch_count();
 
+// Rows [row0, row1) of the multi-GPU finalize over NVLink multicast (mc_*:
+// multicast addresses of symmetric buffers; old_c: this rank's copy).
+int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, const void* old_c,
+                             void* mc_new_c, float* mc_c_sq, void* mc_cext,
+                             unsigned int* mc_shift, float* shift_clear, int64_t row0,
+                             int64_t row1, int64_t D, int dtype, cudaStream_t stream);
+
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,
                     int64_t D, int dtype, cudaStream_t stream);

@@ -64,6 +64,8 @@ _SIGNATURES = {
                                    c_int, c_vp, c_size, c_vp]),
     "fkc_lloyd_iter": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64,
                                c_i64, c_int, c_vp, c_size, c_vp]),
+    "fkc_lloyd_finalize_multimem": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64,
+                                            c_i64, c_i64, c_i64, c_i64, c_int, c_vp]),
     "fkc_lloyd_run": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.c_float,
                               c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_size, c_vp]),
 }

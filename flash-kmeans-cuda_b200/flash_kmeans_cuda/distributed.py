@@ -73,6 +73,116 @@ def allreduce_sums_counts(sums: torch.Tensor, counts: torch.Tensor, group=None) 
     dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
 
 
+def multimem_enabled() -> bool:
+    """FKC_MULTIMEM=0 selects the NCCL all-reduce path for sharded runs."""
+    import os
+
+    return os.environ.get("FKC_MULTIMEM", "1") != "0"
+
+
+class MultimemLloyd:
+    """Data-parallel Lloyd step (points sharded over ranks) whose all-reduce of
+    sums/counts is fused into the finalize over NVLink multicast.
+
+    Workspace, sums, counts, centroids and the shift live in ONE symmetric
+    buffer (torch symmetric memory, same layout on every rank, one multicast
+    object). A step is: ``fkc_lloyd_local`` (local sums/counts) -> barrier ->
+    ``fkc_lloyd_finalize_multimem`` on this rank's slice of the centroid rows
+    (the NVSwitch sums the ranks' copies; new rows go to every rank) ->
+    barrier. No NCCL call per iteration.
+    """
+
+    @staticmethod
+    def available(x_local: torch.Tensor, group=None) -> bool:
+        try:
+            import torch.distributed._symmetric_memory as symm
+        except ImportError:
+            return False
+        if dist.get_backend(group) != "nccl" or int(x_local.shape[-1]) % 4 != 0:
+            return False
+        try:
+            return bool(symm._SymmetricMemory.has_multicast_support(
+                symm.DeviceType.CUDA, x_local.device.index))
+        except Exception:
+            return False
+
+    def __init__(self, x_local: torch.Tensor, n_clusters: int, n_max: int, group=None):
+        import torch.distributed._symmetric_memory as symm
+
+        from . import _C
+        from ._lib import lib
+        from .kmeans import LloydState
+
+        B, N, D = (int(v) for v in x_local.shape)
+        K = int(n_clusters)
+        dev = x_local.device
+        code = _C.dtype_code(x_local)
+        es = x_local.element_size()
+        ws_bytes = int(lib.fkc_lloyd_workspace_size(B, n_max, K, D, code))
+
+        def up(v):
+            return (v + 255) // 256 * 256
+
+        off_ws = 0
+        off_sums = up(off_ws + ws_bytes)
+        off_counts = up(off_sums + B * K * D * 4)
+        off_c = up(off_counts + B * K * 4)
+        off_shift = up(off_c + B * K * D * es)
+        total = up(off_shift + 8)
+        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
+        self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
+        mc = int(self.handle.multicast_ptr)
+        if mc == 0:
+            raise RuntimeError("symmetric memory has no multicast address")
+        self.buf.zero_()
+        b = self.buf
+        self.ws = b[off_ws:off_ws + ws_bytes]
+        self.sums = b[off_sums:off_sums + B * K * D * 4].view(torch.float32).view(B, K, D)
+        self.counts = b[off_counts:off_counts + B * K * 4].view(torch.int32).view(B, K)
+        self.centroids = b[off_c:off_c + B * K * D * es].view(x_local.dtype).view(B, K, D)
+        self.shift = b[off_shift:off_shift + 8].view(torch.float32)
+        self.mc_ws, self.mc_sums, self.mc_counts = mc + off_ws, mc + off_sums, mc + off_counts
+        self.mc_c, self.mc_shift = mc + off_c, mc + off_shift
+        self.state = LloydState(x_local, K, ws=self.ws, sums=self.sums, counts=self.counts)
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        self.rows = shard_bounds(B * K, world, rank)
+        self.dims = (B, K, D, code)
+        self._barrier()
+
+    def _barrier(self) -> None:
+        self.handle.barrier(channel=0, timeout_ms=20000)
+
+    def release(self) -> None:
+        """Ends the symmetric-memory use: every rank passes a last barrier with
+        no kernel of this object in flight before the buffer can be freed."""
+        self._barrier()
+        torch.cuda.synchronize(self.buf.device)
+
+    def set_centroids(self, c: torch.Tensor) -> None:
+        self.centroids.copy_(c)
+        self.state.set_centroids(self.centroids)
+
+    def step(self, it: int, want_shift: bool) -> Optional[torch.Tensor]:
+        """One iteration in place on ``self.centroids``; returns the (1,) shift
+        tensor when ``want_shift`` (valid once the stream reaches it)."""
+        from ._lib import check, lib
+
+        p = it & 1
+        st = self.state
+        st.local(self.centroids)
+        self._barrier()
+        B, K, D, code = self.dims
+        with torch.cuda.device(st.device):
+            check(lib.fkc_lloyd_finalize_multimem(
+                self.mc_sums, self.mc_counts, self.centroids.data_ptr(), self.mc_c, self.mc_ws,
+                (self.mc_shift + 4 * p) if want_shift else None,
+                self.shift[1 - p:2 - p].data_ptr() if want_shift else None,
+                self.rows[0], self.rows[1], B, K, D, code, st._stream()),
+                "fkc_lloyd_finalize_multimem")
+        self._barrier()
+        return self.shift[p:p + 1] if want_shift else None
+
+
 def batch_kmeans_Euclid_sharded(
     x_local: torch.Tensor,
     n_clusters: int,
@@ -123,6 +233,30 @@ def batch_kmeans_Euclid_sharded(
                            group=group)
 
     need_shift = tol > 0 or verbose
+    if (shard == "N" and world > 1 and state_factory is _default_state_factory
+            and multimem_enabled() and MultimemLloyd.available(x_local, group)):
+        n_max = torch.tensor([n_local], device=x_local.device, dtype=torch.int64)
+        dist.all_reduce(n_max, op=dist.ReduceOp.MAX, group=group)
+        mm = MultimemLloyd(x_local, K, int(n_max.item()), group)
+        mm.set_centroids(cur)
+        n_iters_run = 0
+        for it in range(max_iters):
+            sh = mm.step(it, need_shift)
+            n_iters_run = it + 1
+            if need_shift:
+                s = float(sh.item())
+                if verbose and dist.get_rank(group) == 0:
+                    print(f"Iter {it}, center shift: {s:.6f}")
+                if s < tol:
+                    break
+        labels = mm.state.ids
+        cur = mm.centroids.clone()
+        torch.cuda.synchronize(x_local.device)
+        mm.release()
+        if gather:
+            labels = _all_gather_var(labels, dim=1, group=group)
+        return labels, cur, n_iters_run
+
     state = state_factory(x_local, K)
     state.set_centroids(cur)
     nxt = torch.empty_like(cur)

@@ -32,7 +32,11 @@ class LloydState:
     split a step around a reduction of ``sums``/``counts`` (multi-GPU).
     """
 
-    def __init__(self, x: torch.Tensor, n_clusters: int):
+    def __init__(self, x: torch.Tensor, n_clusters: int, *, ws: Optional[torch.Tensor] = None,
+                 sums: Optional[torch.Tensor] = None, counts: Optional[torch.Tensor] = None):
+        """``ws`` (uint8, 256-byte aligned, at least ``fkc_lloyd_workspace_size`` bytes),
+        ``sums`` and ``counts`` may be supplied by the caller (e.g. in symmetric
+        memory for the multi-GPU multicast finalize)."""
         if not x.is_contiguous():
             raise RuntimeError("x must be contiguous")
         self.x = x
@@ -42,12 +46,19 @@ class LloydState:
         self.code = _C.dtype_code(x)
         dev = self.device
         with torch.cuda.device(dev):
-            self.ws_bytes = int(lib.fkc_lloyd_workspace_size(self.B, self.N, self.K, self.D,
-                                                             self.code))
-            self.ws = _C.workspace(self.ws_bytes, dev)
+            need = int(lib.fkc_lloyd_workspace_size(self.B, self.N, self.K, self.D, self.code))
+            if ws is None:
+                self.ws_bytes = need
+                self.ws = _C.workspace(self.ws_bytes, dev)
+            else:
+                if ws.numel() < need:
+                    raise RuntimeError(f"workspace needs {need} bytes (got {ws.numel()})")
+                self.ws, self.ws_bytes = ws, int(ws.numel())
             self.ids = torch.empty((self.B, self.N), dtype=torch.int32, device=dev)
-            self.sums = torch.empty((self.B, self.K, self.D), dtype=torch.float32, device=dev)
-            self.counts = torch.empty((self.B, self.K), dtype=torch.int32, device=dev)
+            self.sums = (sums if sums is not None else
+                         torch.empty((self.B, self.K, self.D), dtype=torch.float32, device=dev))
+            self.counts = (counts if counts is not None else
+                           torch.empty((self.B, self.K), dtype=torch.int32, device=dev))
             self.shift = torch.zeros((1,), dtype=torch.float32, device=dev)
             _lib.check(lib.fkc_lloyd_prepare(x.data_ptr(), self.B, self.N, self.K, self.D,
                                              self.code, self.ws.data_ptr(), self.ws_bytes,

@@ -213,6 +213,31 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
                                    size_t workspace_bytes, fkc_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Multi-GPU finalize fused with the all-reduce, over NVLink multicast
+ * (NVSwitch in-switch reduction). Each rank keeps its per-cluster sums
+ * (B,K,D) fp32 and counts (B,K) int32 from fkc_lloyd_local in symmetric
+ * memory (same layout on every rank, mapped to one multicast object), and the
+ * centroids and Lloyd workspace likewise. After a barrier that follows every
+ * rank's fkc_lloyd_local, each rank calls this for its own slice
+ * [row_begin, row_end) of the B*K centroid rows: it reads the SUM over all
+ * ranks with multimem.ld_reduce from mc_sums / mc_counts (multicast
+ * addresses), computes the new rows from `centroids` (this rank's copy, old
+ * values), and writes them, their ||c||^2 and norm-slice rows into every
+ * rank's centroids and workspace through mc_centroids / mc_workspace
+ * (in place). mc_shift (nullable, multicast u32): max-reduced with the
+ * shift of the slice, as the bits of a non-negative float; shift_clear
+ * (nullable, this rank's copy of a float): set to 0 (a parity double buffer
+ * for the next iteration's shift). A second barrier must follow before any
+ * rank reads the centroids or reuses the sums. D % 4 == 0.
+ * Replaces: the NCCL all-reduce of sums/counts + replicated centroid_finalize
+ * of a data-parallel Lloyd step (kmeans.py:73-105 with sharded x).
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem(
+    const float* mc_sums, const int32_t* mc_counts, const void* centroids, void* mc_centroids,
+    void* mc_workspace, unsigned int* mc_shift, float* shift_clear, int64_t row_begin,
+    int64_t row_end, int64_t B, int64_t K, int64_t D, int dtype, fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * The whole Lloyd loop (batch_kmeans_Euclid without init, kmeans.py:162-195)
  * as ONE CUDA graph launch: a device-side WHILE loop over in-place iterations
  * (assign -> update -> finalize) that stops after max_iters iterations or,

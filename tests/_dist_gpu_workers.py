@@ -10,8 +10,10 @@ import torch
 import torch.distributed as dist
 
 
-def sharded_rank(rank: int, world: int, port: int, shard: str, out_path: str) -> None:
+def sharded_rank(rank: int, world: int, port: int, shard: str, out_path: str,
+                 multimem: bool = True, tol: float = 0.0) -> None:
     os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["FKC_MULTIMEM"] = "1" if multimem else "0"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
@@ -30,8 +32,9 @@ def sharded_rank(rank: int, world: int, port: int, shard: str, out_path: str) ->
     else:
         b0, b1 = shard_bounds(B, world, rank)
         xl, il = x[b0:b1], init[b0:b1]
-    ids, cents, n = batch_kmeans_Euclid_sharded(xl.cuda(), K, max_iters=6, init_centroids=il.cuda(),
-                                                shard=shard, gather=True)
+    ids, cents, n = batch_kmeans_Euclid_sharded(xl.cuda(), K, max_iters=6 if tol == 0 else 40,
+                                                tol=tol, init_centroids=il.cuda(), shard=shard,
+                                                gather=True)
     torch.cuda.synchronize()
     if rank == 0:
         np.savez(out_path, ids=ids.cpu().numpy(), cents=cents.float().cpu().numpy(), n=n)
