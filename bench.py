@@ -512,6 +512,7 @@ def run_ours(args, w: dict) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        MultimemLloyd.release_all()
         dist.destroy_process_group()
 
 

@@ -92,6 +92,36 @@ class MultimemLloyd:
     barrier. No NCCL call per iteration.
     """
 
+    # Symmetric buffers are allocated and rendezvoused once per (group, shapes):
+    # both are collective and cost milliseconds, so repeated runs reuse them.
+    _cache: dict = {}
+
+    @classmethod
+    def cached(cls, x_local: torch.Tensor, n_clusters: int, n_max: int,
+               group=None) -> "MultimemLloyd":
+        """A MultimemLloyd for ``x_local`` whose symmetric buffers are reused
+        across calls with the same group and shapes (x may change)."""
+        from .kmeans import LloydState
+
+        key = (id(group), x_local.device.index, tuple(x_local.shape), x_local.dtype,
+               int(n_clusters), int(n_max))
+        mm = cls._cache.get(key)
+        if mm is None:
+            mm = cls(x_local, n_clusters, n_max, group)
+            cls._cache[key] = mm
+        else:  # per-point terms of this call's x (its contents may have changed)
+            mm.state = LloydState(x_local, int(n_clusters), ws=mm.ws, sums=mm.sums,
+                                  counts=mm.counts)
+        return mm
+
+    @classmethod
+    def release_all(cls) -> None:
+        """Drops the cached buffers (call on every rank, before the process
+        group is destroyed)."""
+        for mm in cls._cache.values():
+            mm.release()
+        cls._cache.clear()
+
     @staticmethod
     def available(x_local: torch.Tensor, group=None) -> bool:
         try:
@@ -237,7 +267,7 @@ def batch_kmeans_Euclid_sharded(
             and multimem_enabled() and MultimemLloyd.available(x_local, group)):
         n_max = torch.tensor([n_local], device=x_local.device, dtype=torch.int64)
         dist.all_reduce(n_max, op=dist.ReduceOp.MAX, group=group)
-        mm = MultimemLloyd(x_local, K, int(n_max.item()), group)
+        mm = MultimemLloyd.cached(x_local, K, int(n_max.item()), group)
         mm.set_centroids(cur)
         n_iters_run = 0
         for it in range(max_iters):
@@ -249,10 +279,8 @@ def batch_kmeans_Euclid_sharded(
                     print(f"Iter {it}, center shift: {s:.6f}")
                 if s < tol:
                     break
-        labels = mm.state.ids
+        labels = mm.state.ids.clone()
         cur = mm.centroids.clone()
-        torch.cuda.synchronize(x_local.device)
-        mm.release()
         if gather:
             labels = _all_gather_var(labels, dim=1, group=group)
         return labels, cur, n_iters_run

@@ -21,7 +21,8 @@ def sharded_rank(rank: int, world: int, port: int, shard: str, out_path: str,
                             timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     from _data import mixture, subset_init
-    from flash_kmeans_cuda.distributed import batch_kmeans_Euclid_sharded, shard_bounds
+    from flash_kmeans_cuda.distributed import (MultimemLloyd, batch_kmeans_Euclid_sharded,
+                                               shard_bounds)
 
     B, N, D, K = (1, 40000, 128, 512) if shard == "N" else (4, 8192, 64, 64)
     x = mixture(B, N, D, K, seed=61, zipf=1.1 if shard == "N" else 0.0)
@@ -39,4 +40,5 @@ def sharded_rank(rank: int, world: int, port: int, shard: str, out_path: str,
     if rank == 0:
         np.savez(out_path, ids=ids.cpu().numpy(), cents=cents.float().cpu().numpy(), n=n)
     dist.barrier()
+    MultimemLloyd.release_all()
     dist.destroy_process_group()
