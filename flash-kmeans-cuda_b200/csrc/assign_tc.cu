@@ -85,6 +85,10 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilog
 constexpr int kEpiWarpBegin = 2;
 constexpr int kParts = kEpiWarps / 4;          // column slices of an item
 constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
+// Split mode partials: 2 slots per CTA x rows of a tile x (f32 score, i32 index).
+constexpr int kSplitMaxCtas = 256;
+constexpr int kSplitMaxRows = 256;
+constexpr size_t kSplitPartialBytes = size_t{2} * kSplitMaxCtas * kSplitMaxRows * 8;
 
 template <int DB, int MT, int NC, int ST, int CG>
 struct Cfg {
@@ -294,6 +298,47 @@ __device__ __forceinline__ void mma_done(uint32_t bar) {
     umma_commit(bar);
 }
 
+// Work of one CTA as segments (tile, chunks [ch0, ch1)). Whole-tile mode:
+// tiles unit, unit + units, ... with all chunks. Split mode (the grid is
+// balanced to the unit: total_tiles x nchunks (tile, chunk) units are cut into
+// `units` contiguous equal ranges, so a tile at a range boundary is shared by
+// two or more CTAs; each writes its partial per-row best to `partials` and
+// splitk_fixup_kernel merges them).
+struct SegIter {
+  bool split;
+  int nchunks, total_tiles, units;
+  int64_t u, u_end;
+  int tile_next;
+
+  __device__ SegIter(bool split_, int nchunks_, int total_tiles_, int unit, int units_)
+      : split(split_), nchunks(nchunks_), total_tiles(total_tiles_), units(units_), u(0),
+        u_end(0), tile_next(unit) {
+    if (split) {
+      const int64_t U = static_cast<int64_t>(total_tiles) * nchunks;
+      u = static_cast<int64_t>(unit) * U / units;
+      u_end = static_cast<int64_t>(unit + 1) * U / units;
+    }
+  }
+
+  __device__ bool next(int& tile, int& ch0, int& ch1) {
+    if (split) {
+      if (u >= u_end) return false;
+      tile = static_cast<int>(u / nchunks);
+      ch0 = static_cast<int>(u - static_cast<int64_t>(tile) * nchunks);
+      const int64_t left = u_end - u;
+      ch1 = left < nchunks - ch0 ? ch0 + static_cast<int>(left) : nchunks;
+      u += ch1 - ch0;
+      return true;
+    }
+    if (tile_next >= total_tiles) return false;
+    tile = tile_next;
+    ch0 = 0;
+    ch1 = nchunks;
+    tile_next += units;
+    return true;
+  }
+};
+
 template <int DB, int MT, int NC, int ST, bool BF16, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     assign_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
@@ -301,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap tm_c,
                      const __grid_constant__ CUtensorMap tm_cext, int32_t* __restrict__ ids,
                      int32_t* __restrict__ counts, int N, int K, int ksteps,
-                     int tiles_per_batch, int total_tiles, int* __restrict__ err) {
+                     int tiles_per_batch, int total_tiles, float* __restrict__ partial_val,
+                     int* __restrict__ partial_idx, int* __restrict__ err) {
   using C = Cfg<DB, MT, NC, ST, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -364,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int nchunks = (K + NC - 1) / NC;
+  const bool split = partial_val != nullptr;  // split mode (CG = 1 only)
 
   // The producer runs its loop with all 32 lanes on warp-uniform values (lane 0
   // waits and issues the TMA loads); the MMA issuer is a single lane. (A warp-
@@ -378,11 +425,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int s = 0; s < MT; ++s) x_last_ph[s] = -1;
     bool ok = true;
-    for (int tile = unit; ok && tile < total_tiles; tile += units) {
+    SegIter seg(split, nchunks, total_tiles, unit, units);
+    int tile, ch0, ch1;
+    while (ok && seg.next(tile, ch0, ch1)) {
       const int b = tile / tiles_per_batch;
       const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
                        static_cast<int>(rank) * MT * kRowsPerSub;
-      for (int ch = 0; ok && ch < nchunks; ++ch) {
+      for (int ch = ch0; ok && ch < ch1; ++ch) {
         const int st = static_cast<int>(c_it % ST);
         const uint32_t ph = (c_it / ST) & 1u;
         if (!warp_wait(C::c_empty(sb, st), ph ^ 1u, abort_flag, lane)) {
@@ -403,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         c_last_ph[st] = static_cast<int>(ph);
         ++c_it;
-        if (ch == 0) {
+        if (ch == ch0) {
 #pragma unroll
           for (int s = 0; s < MT; ++s) {
             if (!warp_wait(C::x_empty(sb, s), (x_it & 1u) ^ 1u, abort_flag, lane)) {
@@ -451,8 +500,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t kHi32 = umma_desc_hi(256, kLayoutSwizzle32B);
       uint32_t c_it = 0, x_it = 0, item = 0;
       bool ok = true;
-      for (int tile = unit; ok && tile < total_tiles; tile += units) {
-        for (int ch = 0; ok && ch < nchunks; ++ch) {
+      SegIter seg(split, nchunks, total_tiles, unit, units);
+      int tile, ch0, ch1;
+      while (ok && seg.next(tile, ch0, ch1)) {
+        for (int ch = ch0; ok && ch < ch1; ++ch) {
           const int st = static_cast<int>(c_it % ST);
           const uint32_t ph = (c_it / ST) & 1u;
           if (!mbar_wait(C::c_full(sb, st), ph, abort_flag)) {
@@ -463,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t c_stage = sb + C::kOffC + st * C::kCStageBytes;
 #pragma unroll
           for (int s = 0; s < MT; ++s) {
-            if (ch == 0 && !mbar_wait(C::x_full(sb, s), x_it & 1u, abort_flag)) {
+            if (ch == ch0 && !mbar_wait(C::x_full(sb, s), x_it & 1u, abort_flag)) {
               raise_abort(abort_flag, err, kErrMmaX);
               ok = false;
               break;
@@ -503,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
                     idesc_ext, 1u);
             mma_done<CG>(C::acc_full(sb, slot));
-            if (ch == nchunks - 1) mma_done<CG>(C::x_empty(sb, s));
+            if (ch == ch1 - 1) mma_done<CG>(C::x_empty(sb, s));
             ++item;
           }
           mma_done<CG>(C::c_empty(sb, st));
@@ -537,7 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         reinterpret_cast<int*>(smem + C::kOffMerge + (kParts - 1) * MT * kRowsPerSub * 4);
     uint32_t item = 0, tcount = 0;
     bool ok = true;
-    for (int tile = unit; ok && tile < total_tiles; tile += units, ++tcount) {
+    SegIter seg(split, nchunks, total_tiles, unit, units);
+    int tile, ch0, ch1;
+    for (bool first_seg = true; ok && seg.next(tile, ch0, ch1); first_seg = false, ++tcount) {
       const int b = tile / tiles_per_batch;
       const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
                        static_cast<int>(rank) * MT * kRowsPerSub;
@@ -548,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         best_val[s] = -INFINITY;
         best_idx[s] = 0;
       }
-      for (int ch = 0; ok && ch < nchunks; ++ch) {
+      for (int ch = ch0; ok && ch < ch1; ++ch) {
         const int col0 = ch * NC + part * NCH;
         const int valid = min(NCH, K - col0);  // may be <= 0 in the last chunk
 #pragma unroll
@@ -627,6 +680,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(C::merge_empty(sb));
+      if (ch0 != 0 || ch1 != nchunks) {
+        // Part of a tile shared with other CTAs (split mode): its per-row best
+        // goes to the partials slot of this CTA's first or last segment.
+        const int slot = 2 * unit + (first_seg ? 0 : 1);
+#pragma unroll
+        for (int s = 0; s < MT; ++s) {
+          const size_t at = static_cast<size_t>(slot) * rows_per_tile + s * kRowsPerSub + row_in_sub;
+          partial_val[at] = best_val[s];
+          partial_idx[at] = best_idx[s];
+        }
+        continue;
+      }
 #pragma unroll
       for (int s = 0; s < MT; ++s) {
         const int row = row0 + s * kRowsPerSub + row_in_sub;
@@ -659,6 +724,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// First unit of CTA c in split mode, and the CTA whose range holds unit u.
+__device__ __forceinline__ int64_t split_u0(int c, int64_t U, int G) {
+  return static_cast<int64_t>(c) * U / G;
+}
+__device__ __forceinline__ int split_cta_of(int64_t u, int64_t U, int G) {
+  int c = static_cast<int>(u * G / U);
+  while (c + 1 < G && split_u0(c + 1, U, G) <= u) ++c;
+  while (c > 0 && split_u0(c, U, G) > u) --c;
+  return c;
+}
+
+// Merges the partial per-row bests of every tile that split mode shared
+// between CTAs and writes its labels (and histogram). One CTA per range
+// boundary c (between CTA c-1 and c); the first boundary inside a tile
+// handles it. Contributors come in ascending column order; ties keep the
+// lower column (the merge compares (truncated score, index) like the kernel).
+__global__ void __launch_bounds__(256) splitk_fixup_kernel(
+    const float* __restrict__ partial_val, const int* __restrict__ partial_idx,
+    int32_t* __restrict__ ids, int32_t* __restrict__ counts, int N, int K, int nchunks,
+    int total_tiles, int tiles_per_batch, int rows_per_tile, int G) {
+  const int c = blockIdx.x + 1;
+  const int64_t U = static_cast<int64_t>(total_tiles) * nchunks;
+  const int64_t u0 = split_u0(c, U, G);
+  if (u0 % nchunks == 0) return;  // the boundary falls between tiles
+  const int t = static_cast<int>(u0 / nchunks);
+  const int64_t t_begin = static_cast<int64_t>(t) * nchunks;
+  if (split_u0(c - 1, U, G) > t_begin) return;  // an earlier boundary is inside t too
+  const int c_first = split_cta_of(t_begin, U, G);
+  const int c_last = split_cta_of(t_begin + nchunks - 1, U, G);
+  const int b = t / tiles_per_batch;
+  const int row0 = (t - b * tiles_per_batch) * rows_per_tile;
+  const int lane = threadIdx.x & 31;
+  for (int base = 0; base < rows_per_tile; base += blockDim.x) {
+    const int r = base + static_cast<int>(threadIdx.x);
+    const bool in_tile = r < rows_per_tile;
+    float best = -INFINITY;
+    int idx = 0;
+    if (in_tile) {
+      for (int cc = c_first; cc <= c_last; ++cc) {
+        const int slot = 2 * cc + (split_u0(cc, U, G) >= t_begin ? 0 : 1);
+        const float v = partial_val[static_cast<size_t>(slot) * rows_per_tile + r];
+        const int i = partial_idx[static_cast<size_t>(slot) * rows_per_tile + r];
+        if (v > best || (v == best && i < idx)) {
+          best = v;
+          idx = i;
+        }
+      }
+    }
+    const int row = row0 + r;
+    const bool valid_row = in_tile && row < N;
+    if (valid_row) ids[static_cast<size_t>(b) * N + row] = idx;
+    if (counts != nullptr) {
+      const uint32_t active = __ballot_sync(0xFFFFFFFFu, valid_row);
+      if (valid_row) {
+        const uint32_t peers = __match_any_sync(active, idx);
+        if (lane == __ffs(peers) - 1)
+          atomicAdd(counts + static_cast<size_t>(b) * K + idx, __popc(peers));
+      }
+    }
+  }
+}
+
 // FKC_ASSIGN_CTA_GROUP=2 selects the CTA-pair kernel; default: single CTAs,
 // which measured as fast or faster on B200 (assign ms, CG=1 vs CG=2: c3 0.831
 // vs 0.827, c2 0.068 vs 0.072, c4 0.117 vs 0.130). The pair kernel halves the
@@ -675,8 +802,8 @@ int cta_group_choice() {
 
 template <int DB, int MT, int NC, int ST, bool BF16, int CG>
 int launch_tc_impl(const void* x, const void* centroids, const void* aext, const void* cext,
-                   int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
-                   cudaStream_t stream) {
+                   int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
+                   int64_t K, int64_t D, cudaStream_t stream) {
   using C = Cfg<DB, MT, NC, ST, CG>;
   auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG>;
   const DeviceInfo* di = nullptr;
@@ -729,49 +856,78 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
     FKC_REQUIRE(pairs > 0, "assign: this device cannot co-schedule 2-CTA clusters");
     units = pairs;
   }
-  const int64_t n_units = std::min<int64_t>(total_tiles, units);
+  int64_t n_units = std::min<int64_t>(total_tiles, units);
+  // Split mode when whole tiles leave the last wave short (c3 on 8 GPUs: 256
+  // tiles on 148 SMs, 86% of the grid busy): the (tile, chunk) units are cut
+  // into one equal range per SM and shared tiles are merged by the fixup.
+  const int64_t nchunks = (K + NC - 1) / NC;
+  float* pval = nullptr;
+  int* pidx = nullptr;
+  if (CG == 1 && splitk_ws != nullptr && nchunks >= 2 && total_tiles % units != 0 &&
+      total_tiles * nchunks >= units && units <= kSplitMaxCtas &&
+      MT * kRowsPerSub <= kSplitMaxRows) {
+    const int64_t waves = (total_tiles + units - 1) / units;
+    const double busy = static_cast<double>(total_tiles) / static_cast<double>(waves * units);
+    if (busy < 0.97) {
+      n_units = units;
+      pval = static_cast<float*>(splitk_ws);
+      pidx = reinterpret_cast<int*>(static_cast<uint8_t*>(splitk_ws) + kSplitPartialBytes / 2);
+    }
+  }
   cfg.gridDim = dim3(static_cast<unsigned>(CG * n_units), 1, 1);
   FKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tm_x, tm_aext, tm_c, tm_cext, ids, counts,
                                   static_cast<int>(N), static_cast<int>(K),
                                   static_cast<int>(D / 16), static_cast<int>(tiles_per_batch),
-                                  static_cast<int>(total_tiles), device_error_word()));
+                                  static_cast<int>(total_tiles), pval, pidx,
+                                  device_error_word()));
   count_launches(1);
+  if (pval != nullptr && n_units > 1) {
+    splitk_fixup_kernel<<<static_cast<unsigned>(n_units - 1), 256, 0, stream>>>(
+        pval, pidx, ids, counts, static_cast<int>(N), static_cast<int>(K),
+        static_cast<int>(nchunks), static_cast<int>(total_tiles),
+        static_cast<int>(tiles_per_batch), static_cast<int>(rows_per_tile),
+        static_cast<int>(n_units));
+    FKC_CUDA_TRY(cudaGetLastError());
+    count_launches(1);
+  }
   return FKC_OK;
 }
 
 template <bool BF16, int CG>
 int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, const void* cext,
-                       int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
-                       cudaStream_t stream) {
+                       int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
+                       int64_t K, int64_t D, cudaStream_t stream) {
   // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
   if constexpr (CG == 2) {
     if (D <= 64)
-      return launch_tc_impl<1, 2, 256, 8, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<1, 2, 256, 8, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
     if (D <= 128)
-      return launch_tc_impl<2, 2, 256, 4, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<2, 2, 256, 4, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
     if (D <= 192)
-      return launch_tc_impl<3, 2, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<3, 2, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
-    return launch_tc_impl<4, 1, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, B, N, K,
+    return launch_tc_impl<4, 1, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K,
                                                  D, stream);
   } else {
     if (D <= 64)
-      return launch_tc_impl<1, 2, 256, 4, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<1, 2, 256, 4, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
     if (D <= 128)
-      return launch_tc_impl<2, 2, 256, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<2, 2, 256, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
     if (D <= 192)
-      return launch_tc_impl<3, 2, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N,
+      return launch_tc_impl<3, 2, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
                                                    K, D, stream);
-    return launch_tc_impl<4, 1, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, B, N, K,
+    return launch_tc_impl<4, 1, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K,
                                                  D, stream);
   }
 }
 
 }  // namespace
+
+size_t assign_splitk_bytes() { return kSplitPartialBytes; }
 
 bool assign_tc_supported(int64_t D, int dtype) {
   if (dtype != FKC_DTYPE_F16 && dtype != FKC_DTYPE_BF16) return false;
@@ -782,19 +938,19 @@ bool assign_tc_supported(int64_t D, int dtype) {
 }
 
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
-                     int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
-                     int dtype, cudaStream_t stream) {
+                     int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
+                     int64_t K, int64_t D, int dtype, cudaStream_t stream) {
   FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
               static_cast<long long>(D), dtype);
   const bool bf16 = dtype == FKC_DTYPE_BF16;
   if (cta_group_choice() == 2)
-    return bf16 ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+    return bf16 ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
                                               stream)
-                : launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+                : launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
                                                stream);
-  return bf16 ? launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+  return bf16 ? launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
                                             stream)
-              : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, B, N, K, D,
+              : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
                                              stream);
 }
 

@@ -170,18 +170,20 @@ size_t assign_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
 }
 
 struct LloydWs {
-  uint8_t* aext = nullptr;  // (B,N,16) bf16, tensor-core path
-  uint8_t* cext = nullptr;  // (B,K,16) bf16, tensor-core path
-  float* c_sq = nullptr;    // (B,K) fp32
+  uint8_t* aext = nullptr;    // (B,N,16) bf16, tensor-core path
+  uint8_t* cext = nullptr;    // (B,K,16) bf16, tensor-core path
+  float* c_sq = nullptr;      // (B,K) fp32
   UpdateWorkspace upd{};
-  LoopCtl* ctl = nullptr;   // whole-loop graph control block
+  LoopCtl* ctl = nullptr;     // whole-loop graph control block
+  uint8_t* splitk = nullptr;  // assign_splitk_bytes(), tensor-core path
 };
 
 constexpr size_t kCtlBytes = 256;
 
 size_t lloyd_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   return assign_ws_bytes(B, N, K, D, dtype) + align_up(static_cast<size_t>(B * K) * 4, 256) +
-         update_workspace_bytes(B, N, K) + kCtlBytes;
+         update_workspace_bytes(B, N, K) + kCtlBytes +
+         (tc_shape_ok(D, dtype) ? assign_splitk_bytes() : 0);
 }
 
 int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
@@ -206,6 +208,8 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
   out->ctl = reinterpret_cast<LoopCtl*>(p);
   p += kCtlBytes;
   if (tc) {
+    out->splitk = p;
+    p += assign_splitk_bytes();
     out->aext = p;
     p += align_up(static_cast<size_t>(B * N) * 32, 256);
   }
@@ -297,7 +301,8 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
     uint8_t* cext = aext + align_up(static_cast<size_t>(B * N) * 32, 256);
     FKC_TRY(launch_xnorm_ext(x, aext, B, N, D, dtype, st));
     FKC_TRY(launch_cnorm_ext(centroids, c_sq, cext, nullptr, B, K, D, dtype, st));
-    return launch_assign_tc(x, centroids, aext, cext, ids, nullptr, B, N, K, D, dtype, st);
+    return launch_assign_tc(x, centroids, aext, cext, ids, nullptr, nullptr, B, N, K, D, dtype,
+                            st);
   }
   return launch_assign_simt(x, centroids, x_sq, c_sq, ids, B, N, K, D, dtype, st);
 }
@@ -393,7 +398,8 @@ FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32
   const cudaStream_t st = as_stream(stream);
   FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
   if (w.aext != nullptr && use_tc(x, centroids, D, dtype))
-    return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, B, N, K, D, dtype, st);
+    return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, w.splitk, B, N, K, D,
+                            dtype, st);
   FKC_TRY(launch_assign_simt(x, centroids, nullptr, w.c_sq, ids, B, N, K, D, dtype, st));
   return launch_histogram(ids, counts, B, N, K, st);
 }

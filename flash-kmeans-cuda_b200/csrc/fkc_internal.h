@@ -86,9 +86,12 @@ int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D,
 int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
                      int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream);
 
+// splitk_ws (nullable, assign_splitk_bytes()): lets the kernel balance an
+// uneven last wave by sharing tiles between CTAs (merged by a fixup kernel).
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
-                     int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K, int64_t D,
-                     int dtype, cudaStream_t stream);
+                     int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
+                     int64_t K, int64_t D, int dtype, cudaStream_t stream);
+size_t assign_splitk_bytes();
 
 int launch_assign_simt(const void* x, const void* centroids, const float* x_sq,
                        const float* c_sq, int32_t* ids, int64_t B, int64_t N, int64_t K,

@@ -37,6 +37,10 @@ def _close_centroids(got, ref, dtype, rel=1e-3):
     (1, 30000, 1024, 128, 1.1),
     (4, 4096, 64, 64, 0.0),
     (1, 5000, 100, 96, 0.0),
+    # fewer row tiles than SMs with several centroid chunks: the assignment
+    # shares tiles between CTAs (split mode) and merges them in a fixup pass
+    (2, 10000, 700, 64, 0.0),
+    (1, 9000, 2000, 128, 1.1),
 ])
 def test_teacher_forced_iterations(cuda_device, dtype, B, N, K, D, zipf):
     from flash_kmeans_cuda.kmeans import LloydState
