@@ -1,5 +1,5 @@
 // CUDA-core assignment for the shapes the tensor-core kernel does not take:
-// fp32 inputs, D not a multiple of 16, D > 256, and devices other than sm_100.
+// fp32 inputs, D not a multiple of 16, D > 384, and devices other than sm_100.
 //
 // Semantics are those of the reference's safe kernel
 // (flash_kmeans_cuda/csrc/assign/assign_safe.cu:38-81 and assign_common.cuh:15-36):

@@ -85,6 +85,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilog
 constexpr int kEpiWarpBegin = 2;
 constexpr int kParts = kEpiWarps / 4;          // column slices of an item
 constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
+constexpr int kMaxTcD = 384;  // D > 256 runs on CTA pairs (each CTA holds half a chunk)
 // Split mode partials: 2 slots per CTA x rows of a tile x (f32 score, i32 index).
 constexpr int kSplitMaxCtas = 256;
 constexpr int kSplitMaxRows = 256;
@@ -931,7 +932,7 @@ size_t assign_splitk_bytes() { return kSplitPartialBytes; }
 
 bool assign_tc_supported(int64_t D, int dtype) {
   if (dtype != FKC_DTYPE_F16 && dtype != FKC_DTYPE_BF16) return false;
-  if (D < 16 || D > 256 || D % 16 != 0) return false;
+  if (D < 16 || D > kMaxTcD || D % 16 != 0) return false;
   const DeviceInfo* di = nullptr;
   if (current_device_info(&di) != FKC_OK) return false;
   return di->cc_major == 10 && di->smem_optin >= static_cast<size_t>(kSmemLimit);
@@ -943,6 +944,22 @@ int launch_assign_tc(const void* x, const void* centroids, const void* aext, con
   FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
               static_cast<long long>(D), dtype);
   const bool bf16 = dtype == FKC_DTYPE_BF16;
+  if (D > 256) {
+    // A single CTA cannot hold a 128-row x sub-tile plus two stages of a
+    // 128-centroid chunk in 227 KB. A CTA pair splits every chunk: each CTA
+    // keeps 64 of its rows (x 96 KB + 2 x 48 KB at D = 384), and the M = 256,
+    // N = 128 MMAs read the same shared-memory bytes per SM as the single-CTA
+    // M = 128, N = 256 ones.
+    if (D <= 320)
+      return bf16 ? launch_tc_impl<5, 1, 128, 2, true, 2>(x, centroids, aext, cext, ids, counts,
+                                                          nullptr, B, N, K, D, stream)
+                  : launch_tc_impl<5, 1, 128, 2, false, 2>(x, centroids, aext, cext, ids, counts,
+                                                           nullptr, B, N, K, D, stream);
+    return bf16 ? launch_tc_impl<6, 1, 128, 2, true, 2>(x, centroids, aext, cext, ids, counts,
+                                                        nullptr, B, N, K, D, stream)
+                : launch_tc_impl<6, 1, 128, 2, false, 2>(x, centroids, aext, cext, ids, counts,
+                                                         nullptr, B, N, K, D, stream);
+  }
   if (cta_group_choice() == 2)
     return bf16 ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
                                               stream)

@@ -137,7 +137,7 @@ namespace {
 // Shape/dtype eligibility of the tensor-core assignment, independent of the
 // device (workspace sizes must not depend on which GPU is current).
 bool tc_shape_ok(int64_t D, int dtype) {
-  return (dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 256 &&
+  return (dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 384 &&
          D % 16 == 0;
 }
 

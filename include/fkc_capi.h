@@ -81,7 +81,7 @@ FKC_CAPI_EXPORT int fkc_device_status(void);
  *   read only by the fp32 / odd-D fallback, which clamps distances at 0 as
  *   the reference's safe kernel does; the tensor-core path ignores it (as the
  *   reference's raw-distance mma path does).
- *   fp16/bf16 with D % 16 == 0 and D <= 256 run the tcgen05 kernel.
+ *   fp16/bf16 with D % 16 == 0 and D <= 384 run the tcgen05 kernel.
  * Replaces: _C.euclid_assign (csrc/bindings.cpp:43-71),
  *           fkc::euclid_assign_out (csrc/api.cpp:58-72),
  *           launch_assign_sm80 / launch_assign_safe (csrc/assign/assign.h:32-44).

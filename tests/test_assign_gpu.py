@@ -4,7 +4,7 @@ Bar (per config): labels identical wherever the top-2 distance gap exceeds
 1e-3 * ||x||^2, and >= 99.9% identical overall. Shapes cover the reference's
 edge cases (tests/test_shapes.py:14-20, tests/test_persistent.py:26-118,
 tests/test_mma_optin.py:35-42): tail tiles, K = 1, K around chunk widths,
-D = 64/96/128/192/256, B > 1.
+D = 64/96/128/192/256/320/384, B > 1.
 """
 
 from __future__ import annotations
@@ -59,6 +59,8 @@ SHAPES = [
     (1, 777, 513, 192),
     (1, 513, 129, 16),
     (1, 2048, 4096, 128),
+    (1, 1500, 300, 320),    # D > 256: CTA-pair kernel, 64 centroid rows per CTA
+    (2, 3000, 700, 384),
 ]
 
 

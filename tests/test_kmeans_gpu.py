@@ -41,6 +41,7 @@ def _close_centroids(got, ref, dtype, rel=1e-3):
     # shares tiles between CTAs (split mode) and merges them in a fixup pass
     (2, 10000, 700, 64, 0.0),
     (1, 9000, 2000, 128, 1.1),
+    (1, 6000, 300, 384, 0.0),  # D > 256 (CTA pairs)
 ])
 def test_teacher_forced_iterations(cuda_device, dtype, B, N, K, D, zipf):
     from flash_kmeans_cuda.kmeans import LloydState
