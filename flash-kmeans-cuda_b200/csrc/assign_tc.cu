@@ -65,6 +65,7 @@
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
+#include "fkc_launch.cuh"
 #include "fkc_ptx.cuh"
 
 namespace fkc {
@@ -410,6 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Everything above is independent of the previous kernel on the stream
+  // (centroids, norm rows and counts come from it).
+  pdl_wait();
   const int nchunks = (K + NC - 1) / NC;
   const bool split = partial_val != nullptr;  // split mode (CG = 1 only)
 
@@ -687,7 +691,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot = 2 * unit + (first_seg ? 0 : 1);
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
-          const size_t at = static_cast<size_t>(slot) * rows_per_tile + s * kRowsPerSub + row_in_sub;
+          const size_t at =
+              static_cast<size_t>(slot) * rows_per_tile + s * kRowsPerSub + row_in_sub;
           partial_val[at] = best_val[s];
           partial_idx[at] = best_idx[s];
         }
@@ -745,6 +750,7 @@ __global__ void __launch_bounds__(256) splitk_fixup_kernel(
     const float* __restrict__ partial_val, const int* __restrict__ partial_idx,
     int32_t* __restrict__ ids, int32_t* __restrict__ counts, int N, int K, int nchunks,
     int total_tiles, int tiles_per_batch, int rows_per_tile, int G) {
+  pdl_wait();
   const int c = blockIdx.x + 1;
   const int64_t U = static_cast<int64_t>(total_tiles) * nchunks;
   const int64_t u0 = split_u0(c, U, G);
@@ -833,6 +839,12 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
+  if constexpr (CG == 1) {  // programmatic dependent launch (see fkc_launch.cuh)
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
@@ -883,13 +895,12 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
                                   device_error_word()));
   count_launches(1);
   if (pval != nullptr && n_units > 1) {
-    splitk_fixup_kernel<<<static_cast<unsigned>(n_units - 1), 256, 0, stream>>>(
-        pval, pidx, ids, counts, static_cast<int>(N), static_cast<int>(K),
-        static_cast<int>(nchunks), static_cast<int>(total_tiles),
-        static_cast<int>(tiles_per_batch), static_cast<int>(rows_per_tile),
-        static_cast<int>(n_units));
-    FKC_CUDA_TRY(cudaGetLastError());
-    count_launches(1);
+    FKC_TRY(launch_pdl(splitk_fixup_kernel, dim3(static_cast<unsigned>(n_units - 1)), dim3(256),
+                       0, stream, static_cast<const float*>(pval),
+                       static_cast<const int*>(pidx), ids, counts, static_cast<int>(N),
+                       static_cast<int>(K), static_cast<int>(nchunks),
+                       static_cast<int>(total_tiles), static_cast<int>(tiles_per_batch),
+                       static_cast<int>(rows_per_tile), static_cast<int>(n_units)));
   }
   return FKC_OK;
 }
@@ -899,31 +910,30 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
                        int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
                        int64_t K, int64_t D, cudaStream_t stream) {
   // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
-  if constexpr (CG == 2) {
-    if (D <= 64)
-      return launch_tc_impl<1, 2, 256, 8, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    if (D <= 128)
-      return launch_tc_impl<2, 2, 256, 4, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    if (D <= 192)
-      return launch_tc_impl<3, 2, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    return launch_tc_impl<4, 1, 256, 2, BF16, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K,
-                                                 D, stream);
-  } else {
-    if (D <= 64)
-      return launch_tc_impl<1, 2, 256, 4, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    if (D <= 128)
-      return launch_tc_impl<2, 2, 256, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    if (D <= 192)
-      return launch_tc_impl<3, 2, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N,
-                                                   K, D, stream);
-    return launch_tc_impl<4, 1, 128, 2, BF16, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K,
-                                                 D, stream);
+#define FKC_TC(DB_, MT_, NC_, ST_, CG_)                                                    \
+  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_>(x, centroids, aext, cext, ids, counts,     \
+                                                (CG_) == 1 ? splitk_ws : nullptr, B, N, K, \
+                                                D, stream)
+  if (D > 256) {
+    // A single CTA cannot hold a 128-row x sub-tile plus two stages of a
+    // 128-centroid chunk in 227 KB. A CTA pair splits every chunk: each CTA
+    // keeps 64 of its rows (x 96 KB + 2 x 48 KB at D = 384), and the M = 256,
+    // N = 128 MMAs read the same shared-memory bytes per SM as the single-CTA
+    // M = 128, N = 256 ones.
+    return D <= 320 ? FKC_TC(5, 1, 128, 2, 2) : FKC_TC(6, 1, 128, 2, 2);
   }
+  if constexpr (CG == 2) {
+    if (D <= 64) return FKC_TC(1, 2, 256, 8, 2);
+    if (D <= 128) return FKC_TC(2, 2, 256, 4, 2);
+    if (D <= 192) return FKC_TC(3, 2, 256, 2, 2);
+    return FKC_TC(4, 1, 256, 2, 2);
+  } else {
+    if (D <= 64) return FKC_TC(1, 2, 256, 4, 1);
+    if (D <= 128) return FKC_TC(2, 2, 256, 2, 1);
+    if (D <= 192) return FKC_TC(3, 2, 128, 2, 1);
+    return FKC_TC(4, 1, 128, 2, 1);
+  }
+#undef FKC_TC
 }
 
 }  // namespace
@@ -944,31 +954,16 @@ int launch_assign_tc(const void* x, const void* centroids, const void* aext, con
   FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
               static_cast<long long>(D), dtype);
   const bool bf16 = dtype == FKC_DTYPE_BF16;
-  if (D > 256) {
-    // A single CTA cannot hold a 128-row x sub-tile plus two stages of a
-    // 128-centroid chunk in 227 KB. A CTA pair splits every chunk: each CTA
-    // keeps 64 of its rows (x 96 KB + 2 x 48 KB at D = 384), and the M = 256,
-    // N = 128 MMAs read the same shared-memory bytes per SM as the single-CTA
-    // M = 128, N = 256 ones.
-    if (D <= 320)
-      return bf16 ? launch_tc_impl<5, 1, 128, 2, true, 2>(x, centroids, aext, cext, ids, counts,
-                                                          nullptr, B, N, K, D, stream)
-                  : launch_tc_impl<5, 1, 128, 2, false, 2>(x, centroids, aext, cext, ids, counts,
-                                                           nullptr, B, N, K, D, stream);
-    return bf16 ? launch_tc_impl<6, 1, 128, 2, true, 2>(x, centroids, aext, cext, ids, counts,
-                                                        nullptr, B, N, K, D, stream)
-                : launch_tc_impl<6, 1, 128, 2, false, 2>(x, centroids, aext, cext, ids, counts,
-                                                         nullptr, B, N, K, D, stream);
-  }
-  if (cta_group_choice() == 2)
-    return bf16 ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
-                                              stream)
-                : launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
-                                               stream);
-  return bf16 ? launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
-                                            stream)
-              : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
-                                             stream);
+  const bool pairs = cta_group_choice() == 2;
+  if (bf16)
+    return pairs ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws,
+                                               B, N, K, D, stream)
+                 : launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, splitk_ws,
+                                               B, N, K, D, stream);
+  return pairs ? launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B,
+                                              N, K, D, stream)
+               : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B,
+                                              N, K, D, stream);
 }
 
 }  // namespace fkc

@@ -12,6 +12,7 @@
 #include <mutex>
 
 #include "fkc_internal.h"
+#include "fkc_launch.cuh"
 
 // Written (atomicCAS from 0) by kernels whose bounded pipeline waits expired.
 __device__ int g_fkc_device_error = 0;
@@ -223,11 +224,11 @@ int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* cou
                     bool counts_ready, const UpdateWorkspace& uw, int64_t B, int64_t N,
                     int64_t K, int64_t D, int dtype, cudaStream_t st) {
   if (!counts_ready) {
-    FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
+    FKC_TRY(launch_zero_fill(counts, static_cast<size_t>(B * K) * 4, st));
     FKC_TRY(launch_histogram(ids, counts, B, N, K, st));
   }
   FKC_TRY(launch_counting_sort(ids, counts, uw, B, N, K, counts_ready, st));
-  FKC_CUDA_TRY(cudaMemsetAsync(sums, 0, static_cast<size_t>(B * K * D) * 4, st));
+  FKC_TRY(launch_zero_fill(sums, static_cast<size_t>(B * K * D) * 4, st));
   return launch_run_accumulate(x, uw.perm, uw.ids_sorted, sums, nullptr, B, N, K, D, dtype, st);
 }
 
@@ -396,7 +397,7 @@ FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32
   LloydWs w;
   FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
   const cudaStream_t st = as_stream(stream);
-  FKC_CUDA_TRY(cudaMemsetAsync(counts, 0, static_cast<size_t>(B * K) * 4, st));
+  FKC_TRY(launch_zero_fill(counts, static_cast<size_t>(B * K) * 4, st));
   if (w.aext != nullptr && use_tc(x, centroids, D, dtype))
     return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, w.splitk, B, N, K, D,
                             dtype, st);

@@ -14,6 +14,7 @@
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
+#include "fkc_launch.cuh"
 
 namespace fkc {
 namespace {
@@ -23,6 +24,7 @@ __global__ void __launch_bounds__(256) finalize_kernel(
     const float* __restrict__ sums, const int32_t* __restrict__ counts,
     const T* __restrict__ old_c, T* __restrict__ new_c, float* __restrict__ c_sq_out,
     uint8_t* __restrict__ cext_out, float* __restrict__ shift_out, int64_t rows, int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(256) finalize_multimem_kernel(
     const float* __restrict__ mc_sums, const int32_t* __restrict__ mc_counts,
     const T* __restrict__ old_c, T* mc_new_c, float* mc_c_sq, uint8_t* mc_cext,
     unsigned int* mc_shift, float* shift_clear, int64_t row0, int64_t row1, int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   if (shift_clear != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *shift_clear = 0.f;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -171,7 +174,36 @@ __global__ void __launch_bounds__(256) finalize_multimem_kernel(
   asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+__global__ void __launch_bounds__(256) zero_fill_kernel(uint32_t* __restrict__ p, int64_t words,
+                                                         bool vec) {
+  pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (vec) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+    for (; i < words / 4; i += stride) q[i] = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    for (; i < words; i += stride) p[i] = 0u;
+  }
+}
+
 }  // namespace
+
+int launch_zero_fill(void* ptr, size_t bytes, cudaStream_t stream) {
+  FKC_REQUIRE(bytes % 4 == 0 && (reinterpret_cast<uintptr_t>(ptr) & 3u) == 0,
+              "zero_fill: 4-byte aligned ranges only");
+  const int64_t words = static_cast<int64_t>(bytes / 4);
+  if (words == 0) return FKC_OK;
+  const bool vec = (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && words % 4 == 0;
+  const DeviceInfo* di = nullptr;
+  FKC_TRY(current_device_info(&di));
+  int64_t grid = ((vec ? words / 4 : words) + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(di->sm_count) * 8;
+  if (grid > cap) grid = cap;
+  if (grid < 1) grid = 1;
+  return launch_pdl(zero_fill_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream,
+                    static_cast<uint32_t*>(ptr), words, vec);
+}
 
 int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, const void* old_c,
                              void* mc_new_c, float* mc_c_sq, void* mc_cext,
@@ -188,36 +220,31 @@ int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, con
   if (grid < 1) grid = 1;
   uint8_t* ce = static_cast<uint8_t*>(mc_cext);
   const int d = static_cast<int>(D);
+  const dim3 g(static_cast<unsigned>(grid)), blk(256);
   switch (dtype) {
     case FKC_DTYPE_F16:
-      finalize_multimem_kernel<__half><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          mc_sums, mc_counts, static_cast<const __half*>(old_c), static_cast<__half*>(mc_new_c),
-          mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
-      break;
+      return launch_pdl(finalize_multimem_kernel<__half>, g, blk, 0, stream, mc_sums, mc_counts,
+                        static_cast<const __half*>(old_c), static_cast<__half*>(mc_new_c),
+                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
     case FKC_DTYPE_BF16:
-      finalize_multimem_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          mc_sums, mc_counts, static_cast<const __nv_bfloat16*>(old_c),
-          static_cast<__nv_bfloat16*>(mc_new_c), mc_c_sq, ce, mc_shift, shift_clear, row0, row1,
-          d);
-      break;
+      return launch_pdl(finalize_multimem_kernel<__nv_bfloat16>, g, blk, 0, stream, mc_sums,
+                        mc_counts, static_cast<const __nv_bfloat16*>(old_c),
+                        static_cast<__nv_bfloat16*>(mc_new_c), mc_c_sq, ce, mc_shift,
+                        shift_clear, row0, row1, d);
     case FKC_DTYPE_F32:
-      finalize_multimem_kernel<float><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          mc_sums, mc_counts, static_cast<const float*>(old_c), static_cast<float*>(mc_new_c),
-          mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
-      break;
+      return launch_pdl(finalize_multimem_kernel<float>, g, blk, 0, stream, mc_sums, mc_counts,
+                        static_cast<const float*>(old_c), static_cast<float*>(mc_new_c),
+                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
     default:
       return set_error(FKC_EINVAL, "finalize_multimem: bad dtype %d", dtype);
   }
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
 }
 
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,
                     int64_t D, int dtype, cudaStream_t stream) {
   const int64_t rows = B * K;
-  if (shift_out != nullptr) FKC_CUDA_TRY(cudaMemsetAsync(shift_out, 0, sizeof(float), stream));
+  if (shift_out != nullptr) FKC_TRY(launch_zero_fill(shift_out, sizeof(float), stream));
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   int64_t grid = (rows + 7) / 8;
@@ -226,28 +253,23 @@ int launch_finalize(const float* sums, const int32_t* counts, const void* old_c,
   if (grid < 1) grid = 1;
   uint8_t* ce = static_cast<uint8_t*>(cext_out);
   const int d = static_cast<int>(D);
+  const dim3 g(static_cast<unsigned>(grid)), blk(256);
   switch (dtype) {
     case FKC_DTYPE_F16:
-      finalize_kernel<__half><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          sums, counts, static_cast<const __half*>(old_c), static_cast<__half*>(new_c), c_sq_out,
-          ce, shift_out, rows, d);
-      break;
+      return launch_pdl(finalize_kernel<__half>, g, blk, 0, stream, sums, counts,
+                        static_cast<const __half*>(old_c), static_cast<__half*>(new_c), c_sq_out,
+                        ce, shift_out, rows, d);
     case FKC_DTYPE_BF16:
-      finalize_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          sums, counts, static_cast<const __nv_bfloat16*>(old_c),
-          static_cast<__nv_bfloat16*>(new_c), c_sq_out, ce, shift_out, rows, d);
-      break;
+      return launch_pdl(finalize_kernel<__nv_bfloat16>, g, blk, 0, stream, sums, counts,
+                        static_cast<const __nv_bfloat16*>(old_c),
+                        static_cast<__nv_bfloat16*>(new_c), c_sq_out, ce, shift_out, rows, d);
     case FKC_DTYPE_F32:
-      finalize_kernel<float><<<static_cast<unsigned>(grid), 256, 0, stream>>>(
-          sums, counts, static_cast<const float*>(old_c), static_cast<float*>(new_c), c_sq_out,
-          ce, shift_out, rows, d);
-      break;
+      return launch_pdl(finalize_kernel<float>, g, blk, 0, stream, sums, counts,
+                        static_cast<const float*>(old_c), static_cast<float*>(new_c), c_sq_out,
+                        ce, shift_out, rows, d);
     default:
       return set_error(FKC_EINVAL, "finalize: bad dtype %d", dtype);
   }
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
 }
 
 }  // namespace fkc

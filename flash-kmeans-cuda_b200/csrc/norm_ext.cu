@@ -7,6 +7,7 @@
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
+#include "fkc_launch.cuh"
 
 namespace fkc {
 namespace {
@@ -41,6 +42,7 @@ __device__ __forceinline__ float warp_row_sumsq(const T* row, int D, int lane) {
 template <typename T>
 __global__ void xnorm_ext_kernel(const T* __restrict__ x, uint8_t* __restrict__ aext,
                                  int64_t rows, int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -57,6 +59,7 @@ template <typename T>
 __global__ void cnorm_ext_kernel(const T* __restrict__ c, const float* __restrict__ c_sq,
                                  uint8_t* __restrict__ cext, float* __restrict__ c_sq_out,
                                  int64_t rows, int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -85,44 +88,35 @@ int grid_for_rows(int64_t rows, int warps_per_block) {
 int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D, int dtype,
                      cudaStream_t stream) {
   const int64_t rows = B * N;
-  const int grid = grid_for_rows(rows, 8);
+  const dim3 grid(grid_for_rows(rows, 8));
   if (dtype == FKC_DTYPE_BF16)
-    xnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(aext), rows,
-        static_cast<int>(D));
-  else
-    xnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(
-        static_cast<const __half*>(x), static_cast<uint8_t*>(aext), rows, static_cast<int>(D));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+    return launch_pdl(xnorm_ext_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream,
+                      static_cast<const __nv_bfloat16*>(x), static_cast<uint8_t*>(aext), rows,
+                      static_cast<int>(D));
+  return launch_pdl(xnorm_ext_kernel<__half>, grid, dim3(256), 0, stream,
+                    static_cast<const __half*>(x), static_cast<uint8_t*>(aext), rows,
+                    static_cast<int>(D));
 }
 
 int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
                      int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream) {
   const int64_t rows = B * K;
-  const int grid = grid_for_rows(rows, 8);
+  const dim3 grid(grid_for_rows(rows, 8));
   uint8_t* ce = static_cast<uint8_t*>(cext);
   const int d = static_cast<int>(D);
   switch (dtype) {
     case FKC_DTYPE_BF16:
-      cnorm_ext_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(centroids), c_sq, ce, c_sq_out, rows, d);
-      break;
+      return launch_pdl(cnorm_ext_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream,
+                        static_cast<const __nv_bfloat16*>(centroids), c_sq, ce, c_sq_out, rows, d);
     case FKC_DTYPE_F16:
-      cnorm_ext_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<const __half*>(centroids),
-                                                         c_sq, ce, c_sq_out, rows, d);
-      break;
+      return launch_pdl(cnorm_ext_kernel<__half>, grid, dim3(256), 0, stream,
+                        static_cast<const __half*>(centroids), c_sq, ce, c_sq_out, rows, d);
     case FKC_DTYPE_F32:
-      cnorm_ext_kernel<float><<<grid, 256, 0, stream>>>(static_cast<const float*>(centroids),
-                                                        c_sq, ce, c_sq_out, rows, d);
-      break;
+      return launch_pdl(cnorm_ext_kernel<float>, grid, dim3(256), 0, stream,
+                        static_cast<const float*>(centroids), c_sq, ce, c_sq_out, rows, d);
     default:
       return set_error(FKC_EINVAL, "bad dtype %d", dtype);
   }
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
 }
 
 }  // namespace fkc

@@ -28,6 +28,7 @@
 
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
+#include "fkc_launch.cuh"
 
 namespace fkc {
 namespace {
@@ -42,6 +43,7 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 
 __global__ void histogram_kernel(const int32_t* __restrict__ ids, int32_t* __restrict__ counts,
                                  int64_t total, int64_t N, int K) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
@@ -73,6 +75,7 @@ template <int V>
 __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int32_t* __restrict__ counts,
                                                             int32_t* __restrict__ offsets,
                                                             int32_t* __restrict__ cursor, int K) {
+  pdl_wait();
   __shared__ int warp_tot[kScanThreads / 32];
   __shared__ int carry_s;
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -152,6 +155,7 @@ template <int RPT>
 __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
     const int32_t* __restrict__ ids, int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
     int32_t* __restrict__ ids_sorted, int N, int K, int chunks_per_batch) {
+  pdl_wait();
   extern __shared__ int cnt[];  // K counters, then reused for the K slot bases
   const int t = threadIdx.x;
   const int b = blockIdx.x / chunks_per_batch;
@@ -199,6 +203,7 @@ __global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
                                       int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
                                       int32_t* __restrict__ ids_sorted, int64_t total, int64_t N,
                                       int K) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
@@ -289,6 +294,7 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
     const int32_t* __restrict__ ids_sorted, float* __restrict__ sums,
     int32_t* __restrict__ counts, int N, int K, int spans_per_batch, int span_len,
     int64_t total_spans) {
+  pdl_wait();
   constexpr int kVec = 16 / sizeof(T);
   constexpr int R = 2 * L;  // positions per stream per 64-position segment
   static_assert(32 % L == 0 && R % P == 0, "stream layout");
@@ -409,6 +415,7 @@ __global__ void __launch_bounds__(256) run_accumulate_vec_kernel(
     const int32_t* __restrict__ ids_sorted, float* __restrict__ sums,
     int32_t* __restrict__ counts, int N, int K, int D, int L, int ranges_per_batch,
     int64_t total_ranges) {
+  pdl_wait();
   constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte vector
   const int lane = threadIdx.x & 31;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -478,7 +485,8 @@ __global__ void __launch_bounds__(256) run_accumulate_vec_kernel(
       if (sub == 0) {
         float* dst = sums + (static_cast<size_t>(b) * K + id) * D + v * kVec;
 #pragma unroll
-        for (int k = 0; k < kVec; k += 4) red_add_v4(dst + k, acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
+        for (int k = 0; k < kVec; k += 4)
+          red_add_v4(dst + k, acc[k], acc[k + 1], acc[k + 2], acc[k + 3]);
       }
       if (counts != nullptr && lane == 0)
         atomicAdd(counts + static_cast<size_t>(b) * K + id, end - pos);
@@ -494,6 +502,7 @@ __global__ void __launch_bounds__(256) run_accumulate_scalar_kernel(
     const int32_t* __restrict__ ids_sorted, float* __restrict__ sums,
     int32_t* __restrict__ counts, int N, int K, int D, int ranges_per_batch,
     int64_t total_ranges) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (gw >= total_ranges) return;
@@ -575,12 +584,9 @@ int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, fl
   spans_per_batch = (N + span_len - 1) / span_len;
   const int64_t total = spans_per_batch * B;
   const int64_t blocks = std::min<int64_t>((total + 7) / 8, cap);
-  kern<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-      x, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
-      static_cast<int>(spans_per_batch), static_cast<int>(span_len), total);
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, perm,
+                    ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
+                    static_cast<int>(spans_per_batch), static_cast<int>(span_len), total);
 }
 
 template <typename T>
@@ -608,17 +614,15 @@ int run_accumulate_typed(const void* x, const int32_t* perm, const int32_t* ids_
       default:
         break;
     }
-    run_accumulate_vec_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        xt, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
-        static_cast<int>(D), L, static_cast<int>(ranges_per_batch), total);
-  } else {
-    run_accumulate_scalar_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        xt, perm, ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
-        static_cast<int>(D), static_cast<int>(ranges_per_batch), total);
+    return launch_pdl(run_accumulate_vec_kernel<T>, dim3(static_cast<unsigned>(blocks)), dim3(256),
+                      0, stream, xt, perm, ids_sorted, sums, counts, static_cast<int>(N),
+                      static_cast<int>(K), static_cast<int>(D), L,
+                      static_cast<int>(ranges_per_batch), total);
   }
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+  return launch_pdl(run_accumulate_scalar_kernel<T>, dim3(static_cast<unsigned>(blocks)),
+                    dim3(256), 0, stream, xt, perm, ids_sorted, sums, counts, static_cast<int>(N),
+                    static_cast<int>(K), static_cast<int>(D), static_cast<int>(ranges_per_batch),
+                    total);
 }
 
 }  // namespace
@@ -644,11 +648,8 @@ UpdateWorkspace carve_update_workspace(void* ws, int64_t B, int64_t N, int64_t K
 int launch_histogram(const int32_t* ids, int32_t* counts, int64_t B, int64_t N, int64_t K,
                      cudaStream_t stream) {
   const int64_t total = B * N;
-  histogram_kernel<<<grid_for(total, 256), 256, 0, stream>>>(ids, counts, total, N,
-                                                             static_cast<int>(K));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+  return launch_pdl(histogram_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream, ids,
+                    counts, total, N, static_cast<int>(K));
 }
 
 namespace {
@@ -662,12 +663,9 @@ int launch_scatter_chunk(const int32_t* ids, const UpdateWorkspace& w, int64_t B
     FKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int64_t chunks = (N + kSortThreads * RPT - 1) / (kSortThreads * RPT);
   FKC_REQUIRE(chunks * B < (1ll << 31), "update: too many row chunks");
-  kern<<<static_cast<unsigned>(chunks * B), kSortThreads, smem, stream>>>(
-      ids, w.cursor, w.perm, w.ids_sorted, static_cast<int>(N), static_cast<int>(K),
-      static_cast<int>(chunks));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+  return launch_pdl(kern, dim3(static_cast<unsigned>(chunks * B)), dim3(kSortThreads),
+                    static_cast<size_t>(smem), stream, ids, w.cursor, w.perm, w.ids_sorted,
+                    static_cast<int>(N), static_cast<int>(K), static_cast<int>(chunks));
 }
 
 }  // namespace
@@ -677,13 +675,11 @@ int launch_counting_sort(const int32_t* ids, const int32_t* counts, const Update
   FKC_REQUIRE(B <= 2147483647ll && N <= 2147483647ll && K <= 2147483647ll,
               "update: sizes out of range");
   if (K % 4 == 0)
-    scan_kernel<4><<<static_cast<unsigned>(B), kScanThreads, 0, stream>>>(
-        counts, w.offsets, w.cursor, static_cast<int>(K));
+    FKC_TRY(launch_pdl(scan_kernel<4>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads), 0,
+                       stream, counts, w.offsets, w.cursor, static_cast<int>(K)));
   else
-    scan_kernel<1><<<static_cast<unsigned>(B), kScanThreads, 0, stream>>>(
-        counts, w.offsets, w.cursor, static_cast<int>(K));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
+    FKC_TRY(launch_pdl(scan_kernel<1>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads), 0,
+                       stream, counts, w.offsets, w.cursor, static_cast<int>(K)));
   // With labels outside [0,K) some sorted positions stay unwritten: they must
   // read as label -1, which the accumulator skips.
   if (!all_valid)
@@ -699,11 +695,8 @@ int launch_counting_sort(const int32_t* ids, const int32_t* counts, const Update
     return launch_scatter_chunk<1>(ids, w, B, N, K, stream);
   }
   const int64_t total = B * N;
-  scatter_atomic_kernel<<<grid_for(total, 256), 256, 0, stream>>>(
-      ids, w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K));
-  FKC_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return FKC_OK;
+  return launch_pdl(scatter_atomic_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream, ids,
+                    w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K));
 }
 
 int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids_sorted,
