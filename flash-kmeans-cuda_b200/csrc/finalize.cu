@@ -12,6 +12,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
 #include "fkc_launch.cuh"
@@ -51,6 +53,64 @@ __global__ void __launch_bounds__(256) finalize_kernel(
       if (cext_out != nullptr) write_norm_ext(cext_out + r * kNormExtBytes, -0.5f * sq, false);
       if (shift_out != nullptr)
         atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(sqrtf(sh)));
+    }
+  }
+}
+
+// Vector variant for D % 4 == 0 and aligned rows: L lanes per centroid row
+// (32/L rows per warp), each lane 4 consecutive features per step (16-byte
+// sums loads, 8- or 16-byte centroid loads/stores); one shift atomic per warp.
+template <typename T, int L>
+__global__ void __launch_bounds__(256) finalize_vec_kernel(
+    const float* __restrict__ sums, const int32_t* __restrict__ counts,
+    const T* __restrict__ old_c, T* __restrict__ new_c, float* __restrict__ c_sq_out,
+    uint8_t* __restrict__ cext_out, float* __restrict__ shift_out, int64_t rows, int D) {
+  pdl_wait();
+  constexpr int G = 32 / L;  // rows per warp
+  using V = typename std::conditional<sizeof(T) == 2, uint2, uint4>::type;  // 4 elements
+  const int lane = threadIdx.x & 31;
+  const int g = lane / L, i = lane % L;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * G;
+       r0 < rows; r0 += warps_total * G) {
+    const int64_t r = r0 + g;
+    const bool on = r < rows;
+    float sq = 0.f, sh = 0.f;
+    if (on) {
+      const int32_t cnt = counts[r];
+      const float fc = static_cast<float>(cnt);
+      for (int d = 4 * i; d < D; d += 4 * L) {
+        const float4 sv = *reinterpret_cast<const float4*>(sums + r * D + d);
+        const V ov = *reinterpret_cast<const V*>(old_c + r * D + d);
+        const T* o = reinterpret_cast<const T*>(&ov);
+        const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+        V nvv;
+        T* nv = reinterpret_cast<T*>(&nvv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          nv[e] = cnt > 0 ? from_f32<T>(__fdiv_rn(s4[e], fc)) : o[e];
+          const float nf = to_f32<T>(nv[e]);
+          const float df = nf - to_f32<T>(o[e]);
+          sq = fmaf(nf, nf, sq);
+          sh = fmaf(df, df, sh);
+        }
+        *reinterpret_cast<V*>(new_c + r * D + d) = nvv;
+      }
+    }
+#pragma unroll
+    for (int off = L / 2; off >= 1; off >>= 1) {
+      sq += __shfl_xor_sync(0xFFFFFFFFu, sq, off);
+      sh += __shfl_xor_sync(0xFFFFFFFFu, sh, off);
+    }
+    if (on && i == 0) {
+      if (c_sq_out != nullptr) c_sq_out[r] = sq;
+      if (cext_out != nullptr) write_norm_ext(cext_out + r * kNormExtBytes, -0.5f * sq, false);
+    }
+    if (shift_out != nullptr) {
+      float m = on ? sqrtf(sh) : 0.f;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+      if (lane == 0) atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(m));
     }
   }
 }
@@ -254,6 +314,38 @@ int launch_finalize(const float* sums, const int32_t* counts, const void* old_c,
   uint8_t* ce = static_cast<uint8_t*>(cext_out);
   const int d = static_cast<int>(D);
   const dim3 g(static_cast<unsigned>(grid)), blk(256);
+  const size_t es = dtype == FKC_DTYPE_F32 ? 4 : 2;
+  const bool vec = D % 4 == 0 && (reinterpret_cast<uintptr_t>(sums) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(old_c) & (4 * es - 1)) == 0 &&
+                   (reinterpret_cast<uintptr_t>(new_c) & (4 * es - 1)) == 0;
+  if (vec) {
+    const int L = D <= 32 ? 8 : (D <= 64 ? 16 : 32);  // lanes per row
+    const int64_t warps = (rows * L + 31) / 32;
+    int64_t gv = (warps + 7) / 8;
+    if (gv > cap) gv = cap;
+    const dim3 gg(static_cast<unsigned>(gv < 1 ? 1 : gv));
+    auto go = [&](auto tag, auto lanes) -> int {
+      using T = decltype(tag);
+      return launch_pdl(finalize_vec_kernel<T, decltype(lanes)::value>, gg, blk, 0, stream, sums,
+                        counts, static_cast<const T*>(old_c), static_cast<T*>(new_c), c_sq_out,
+                        ce, shift_out, rows, d);
+    };
+    using L8 = std::integral_constant<int, 8>;
+    using L16 = std::integral_constant<int, 16>;
+    using L32 = std::integral_constant<int, 32>;
+    switch (dtype) {
+      case FKC_DTYPE_F16:
+        return L == 8 ? go(__half{}, L8{}) : L == 16 ? go(__half{}, L16{}) : go(__half{}, L32{});
+      case FKC_DTYPE_BF16:
+        return L == 8    ? go(__nv_bfloat16{}, L8{})
+               : L == 16 ? go(__nv_bfloat16{}, L16{})
+                         : go(__nv_bfloat16{}, L32{});
+      case FKC_DTYPE_F32:
+        return L == 8 ? go(float{}, L8{}) : L == 16 ? go(float{}, L16{}) : go(float{}, L32{});
+      default:
+        return set_error(FKC_EINVAL, "finalize: bad dtype %d", dtype);
+    }
+  }
   switch (dtype) {
     case FKC_DTYPE_F16:
       return launch_pdl(finalize_kernel<__half>, g, blk, 0, stream, sums, counts,
