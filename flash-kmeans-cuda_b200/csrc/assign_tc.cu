@@ -105,22 +105,33 @@ struct Cfg {
   static constexpr int kOffAext = kOffC + ST * kCStageBytes;
   static constexpr int kOffCext = kOffAext + MT * kAextSubBytes;
   static constexpr int kOffBar = kOffCext + ST * kCextStageBytes;
-  // x_full[MT] x_empty[MT] c_full[ST] c_empty[ST] acc_full[2] acc_empty[2] drain
-  // merge_full merge_empty
-  static constexpr int kNumBars = 2 * MT + 2 * ST + 7;
+  // Accumulator slots: all 512 TMEM columns, NC columns each (2 or 4 slots).
+  static constexpr int kSlots = 512 / NC;
+  // Epilogue ownership: with two sub-tiles per tile, each half of the epilogue
+  // warps can own one sub-tile (all NC columns of its items); otherwise the
+  // halves split the columns of every item and exchange per-row bests. Owning
+  // holds a 256-column slot while the first 128 columns are reduced (only 128
+  // fit in registers), which stalls the MMA when an item's MMA is long: on
+  // B200 it is faster for D <= 64 (c4 assign 123 -> 100 us) and slower at
+  // D = 128 (c3 0.853 -> 0.902 ms), so it is used for short items only.
+  static constexpr bool kOwn = MT == kParts && (DB == 1 || NC == 128);
+  // x_full[MT] x_empty[MT] c_full[ST] c_empty[ST] acc_full[kSlots]
+  // acc_empty[kSlots] drain merge_full[kParts] merge_empty[kParts]
+  static constexpr int kNumBars = 2 * MT + 2 * ST + 2 * kSlots + 1 + 2 * kParts;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  // best per row of column slices 1..kParts-1: (kParts-1) x MT*128 x (f32, i32)
+  // per-row bests exchanged between column slices: (sender, sub) x 128 x (f32, i32)
   static constexpr int kOffMerge = kOffMisc + 16;
   static constexpr int kSmemBytes =
-      kOffMerge + (kParts - 1) * MT * kRowsPerSub * 8 + 1024;  // + alignment slack
+      kOffMerge + kParts * MT * kRowsPerSub * 8 + 1024;  // + alignment slack
   // bytes landing on a full barrier per phase (both CTAs for CG = 2)
   static constexpr uint32_t kXTxBytes = CG * (kXSubBytes + kAextSubBytes);
   static constexpr uint32_t kCTxBytes = CG * (kCStageBytes + kCextStageBytes);
-  static constexpr uint32_t kTmemCols = 2 * NC;
+  static constexpr uint32_t kTmemCols = kSlots * NC;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget exceeded");
   static_assert(NC % 32 == 0 && NC >= 32 && NC <= 256, "UMMA N");
   static_assert(kNB % 16 == 0, "TMA box rows / UMMA N granularity");
-  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+  static_assert(NC == 128 || NC == 256, "accumulator slots tile the 512 TMEM columns");
+  static_assert(kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
 
   __device__ static uint32_t x_full(uint32_t base, int s) { return base + kOffBar + 8 * s; }
@@ -135,16 +146,17 @@ struct Cfg {
     return base + kOffBar + 8 * (2 * MT + 2 * ST + a);
   }
   __device__ static uint32_t acc_empty(uint32_t base, int a) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 + a);
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + kSlots + a);
   }
   __device__ static uint32_t drain(uint32_t base) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 4);
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots);
   }
-  __device__ static uint32_t merge_full(uint32_t base) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 5);
+  // Bests sent by slice p are ready / have been consumed.
+  __device__ static uint32_t merge_full(uint32_t base, int p) {
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots + 1 + p);
   }
-  __device__ static uint32_t merge_empty(uint32_t base) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 6);
+  __device__ static uint32_t merge_empty(uint32_t base, int p) {
+    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots + 1 + kParts + p);
   }
 };
 
@@ -300,6 +312,22 @@ __device__ __forceinline__ void mma_done(uint32_t bar) {
     umma_commit(bar);
 }
 
+// Label of one x row (a warp writes 32 consecutive rows) and its histogram
+// count: lanes with the same label add once, with the number of such lanes.
+__device__ __forceinline__ void write_label(int32_t* __restrict__ ids, int32_t* __restrict__ counts,
+                                            int b, int N, int K, int row, int idx, int lane) {
+  const bool valid_row = row < N;
+  if (valid_row) ids[static_cast<size_t>(b) * N + row] = idx;
+  if (counts != nullptr) {
+    const uint32_t active = __ballot_sync(0xFFFFFFFFu, valid_row);
+    if (valid_row) {
+      const uint32_t peers = __match_any_sync(active, idx);
+      if (lane == __ffs(peers) - 1)
+        atomicAdd(counts + static_cast<size_t>(b) * K + idx, __popc(peers));
+    }
+  }
+}
+
 // Work of one CTA as segments (tile, chunks [ch0, ch1)). Whole-tile mode:
 // tiles unit, unit + units, ... with all chunks. Split mode (the grid is
 // balanced to the unit: total_tiles x nchunks (tile, chunk) units are cut into
@@ -379,13 +407,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(C::c_full(sb, st), 1);
       mbar_init(C::c_empty(sb, st), 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < C::kSlots; ++a) {
       mbar_init(C::acc_full(sb, a), 1);
-      mbar_init(C::acc_empty(sb, a), CG * kEpiWarps);  // one arrival per epilogue warp
+      // one arrival per epilogue warp that reads the slot (of both CTAs of a pair)
+      mbar_init(C::acc_empty(sb, a), CG * (C::kOwn ? 4 : kEpiWarps));
     }
     mbar_init(C::drain(sb), 1);
-    mbar_init(C::merge_full(sb), kEpiWarps - 4);  // the warps of column slices 1..
-    mbar_init(C::merge_empty(sb), 4);             // the four warps of slice 0
+    for (int p = 0; p < kParts; ++p) {
+      mbar_init(C::merge_full(sb, p), 4);   // the four warps of the sending slice
+      mbar_init(C::merge_empty(sb, p), 4);  // the four warps of the receiving slice
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -524,8 +555,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
-            const uint32_t slot = item & 1u;
-            if (!mbar_wait(C::acc_empty(sb, slot), ((item >> 1) & 1u) ^ 1u, abort_flag)) {
+            const uint32_t slot = item % C::kSlots;
+            if (!mbar_wait(C::acc_empty(sb, slot), ((item / C::kSlots) & 1u) ^ 1u, abort_flag)) {
               raise_abort(abort_flag, err, kErrMmaAcc);
               ok = false;
               break;
@@ -574,31 +605,148 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(C::drain(sb));
       mbar_wait(C::drain(sb), 0u, abort_flag, ok ? kWaitDeadlineNs : 100000000ull);
     }
+  } else if constexpr (C::kOwn) {
+    // ------------------------------------------- epilogue, sub-tile owners
+    // Warps of half p read all NC columns of the items of sub-tile p (one x
+    // row per thread, TMEM lane quarter = warp % 4) and keep that row's best
+    // over the whole sweep, so no per-tile merge is needed. The two warps on
+    // each SM sub-partition belong to different halves and so work on items
+    // one MMA apart instead of in lockstep.
+    constexpr int kBatch = 128;  // columns held in registers at once
+    static_assert(NC % kBatch == 0, "whole register batches per item");
+    const int part = (warp - kEpiWarpBegin) >> 2;  // = the sub-tile owned
+    const int q = warp & 3;
+    const int row_in_sub = q * 32 + lane;
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t item = 0;
+    bool ok = true;
+    SegIter seg(split, nchunks, total_tiles, unit, units);
+    int tile, ch0, ch1;
+    for (bool first_seg = true; ok && seg.next(tile, ch0, ch1); first_seg = false) {
+      const int b = tile / tiles_per_batch;
+      const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
+                       static_cast<int>(rank) * MT * kRowsPerSub;
+      float best_val = -INFINITY;
+      int best_idx = 0;
+      for (int ch = ch0; ok && ch < ch1; ++ch) {
+#pragma unroll
+        for (int s = 0; s < MT; ++s, ++item) {
+          if (s != part) continue;
+          const uint32_t slot = item % C::kSlots;
+          int got = 1;
+          if (lane == 0) got = mbar_wait(C::acc_full(sb, slot), (item / C::kSlots) & 1u, abort_flag);
+          got = __shfl_sync(0xFFFFFFFFu, got, 0);
+          if (!got) {
+            if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int h = 0; h < NC / kBatch; ++h) {
+            const int col0 = ch * NC + h * kBatch;
+            const int valid = min(kBatch, K - col0);  // may be <= 0 in the last chunk
+            uint32_t r[kBatch / 32][32];
+            if (valid > 0) epilogue_load<kBatch>(lane_addr + slot * NC + h * kBatch, r);
+            if (h == NC / kBatch - 1) {
+              // The last columns are in registers: release the slot to the MMA.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) {
+                if (CG == 1 || leader)
+                  mbar_arrive(C::acc_empty(sb, slot));
+                else
+                  mbar_arrive_cluster_relaxed(C::acc_empty(sb_lead, slot));
+              }
+            }
+            if (valid >= kBatch)
+              epilogue_reduce<kBatch, false>(r, valid, col0, best_val, best_idx);
+            else if (valid > 0)
+              epilogue_reduce<kBatch, true>(r, valid, col0, best_val, best_idx);
+          }
+        }
+      }
+      if (!ok) break;
+      if (ch0 != 0 || ch1 != nchunks) {
+        // Part of a tile shared with other CTAs (split mode).
+        const int pslot = 2 * unit + (first_seg ? 0 : 1);
+        const size_t at =
+            static_cast<size_t>(pslot) * rows_per_tile + part * kRowsPerSub + row_in_sub;
+        partial_val[at] = best_val;
+        partial_idx[at] = best_idx;
+        continue;
+      }
+      write_label(ids, counts, b, N, K, row0 + part * kRowsPerSub + row_in_sub, best_idx, lane);
+    }
   } else {
     // ----------------------------------------------------------- epilogue
-    // kParts warpgroups: slice p reads columns [p*NCH, (p+1)*NCH) of every item
-    // for all 128 TMEM lanes (one x row per thread). At the end of a tile the
-    // slices 1.. hand their per-row best to slice 0 through shared memory
-    // (bounded mbarrier handshake) and slice 0 writes the labels.
+    // Two column slices: slice p reads columns [p*NCH, (p+1)*NCH) of every item
+    // for all 128 TMEM lanes (one x row per thread). Sub-tile s is finished
+    // (labels, histogram) by slice s % 2, which takes the other slice's per-row
+    // best for it through shared memory. A finished tile waits in registers and
+    // is merged and written once the first item of the next tile has been
+    // released to the MMA and reduced: neither slice waits for the
+    // other at a tile boundary, and with two sub-tiles both share the work.
+    // (The merge runs after that item's reduction, when its 128 score
+    // registers are free.)
+    static_assert(kParts == 2, "one peer slice");
     constexpr int NCH = NC / kParts;
     static_assert(NCH % 32 == 0, "each epilogue slice reads whole 32-column groups");
-    const int epi = warp - kEpiWarpBegin;
-    const int part = epi >> 2;
+    const int part = (warp - kEpiWarpBegin) >> 2;
+    const int peer = part ^ 1;
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_sub = q * 32 + lane;
     const uint32_t lane_addr =
         tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(part * NCH);
     float* merge_val = reinterpret_cast<float*>(smem + C::kOffMerge);
     int* merge_idx =
-        reinterpret_cast<int*>(smem + C::kOffMerge + (kParts - 1) * MT * kRowsPerSub * 4);
-    uint32_t item = 0, tcount = 0;
+        reinterpret_cast<int*>(smem + C::kOffMerge + kParts * MT * kRowsPerSub * 4);
+    const bool owns = part < MT;             // finishes sub-tile `part`
+    const bool sends = MT > 1 || part == 1;  // sends its bests of the other sub-tile(s)
+    // The finished tile waiting for the peer's bests (pend_tile < 0: none).
+    int pend_tile = -1, pend_pslot = -1, pend_idx = 0;
+    float pend_val = -INFINITY;
+    uint32_t tcount = 0;
+    // Merges the peer's bests into the pending tile's sub-tile `part` and
+    // writes its labels (or split-mode partials). Called once the tile counter
+    // has moved past the pending tile.
+    auto finish = [&]() -> bool {
+      int got = 1;
+      if (lane == 0) got = mbar_wait(C::merge_full(sb, peer), (tcount & 1u) ^ 1u, abort_flag);
+      got = __shfl_sync(0xFFFFFFFFu, got, 0);
+      if (!got) {
+        if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
+        return false;
+      }
+      const int at_m = (peer * MT + part) * kRowsPerSub + row_in_sub;
+      const float v1 = merge_val[at_m];
+      const int i1 = merge_idx[at_m];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(C::merge_empty(sb, peer));
+      if (v1 > pend_val || (v1 == pend_val && i1 < pend_idx)) {
+        pend_val = v1;
+        pend_idx = i1;
+      }
+      if (pend_pslot >= 0) {
+        const size_t at = static_cast<size_t>(pend_pslot) * rows_per_tile + part * kRowsPerSub +
+                          row_in_sub;
+        partial_val[at] = pend_val;
+        partial_idx[at] = pend_idx;
+      } else {
+        const int pb = pend_tile / tiles_per_batch;
+        const int prow = (pend_tile - pb * tiles_per_batch) * rows_per_tile +
+                         static_cast<int>(rank) * MT * kRowsPerSub + part * kRowsPerSub +
+                         row_in_sub;
+        write_label(ids, counts, pb, N, K, prow, pend_idx, lane);
+      }
+      pend_tile = -1;
+      return true;
+    };
+    uint32_t item = 0;
     bool ok = true;
     SegIter seg(split, nchunks, total_tiles, unit, units);
     int tile, ch0, ch1;
     for (bool first_seg = true; ok && seg.next(tile, ch0, ch1); first_seg = false, ++tcount) {
-      const int b = tile / tiles_per_batch;
-      const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
-                       static_cast<int>(rank) * MT * kRowsPerSub;
       float best_val[MT];
       int best_idx[MT];
 #pragma unroll
@@ -611,9 +759,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int valid = min(NCH, K - col0);  // may be <= 0 in the last chunk
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
-          const uint32_t slot = item & 1u;
+          const uint32_t slot = item % C::kSlots;
           int got = 1;
-          if (lane == 0) got = mbar_wait(C::acc_full(sb, slot), (item >> 1) & 1u, abort_flag);
+          if (lane == 0) got = mbar_wait(C::acc_full(sb, slot), (item / C::kSlots) & 1u, abort_flag);
           got = __shfl_sync(0xFFFFFFFFu, got, 0);
           if (!got) {
             if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
@@ -641,80 +789,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           else if (valid > 0)
             epilogue_reduce<NCH, true>(r, valid, col0, best_val[s], best_idx[s]);
           ++item;
+          if (pend_tile >= 0 && !finish()) {
+            ok = false;
+            break;
+          }
         }
       }
       if (!ok) break;
       const uint32_t mph = tcount & 1u;
-      if (part > 0) {
+      if (sends) {
         int got = 1;
-        if (lane == 0) got = mbar_wait(C::merge_empty(sb), mph ^ 1u, abort_flag);
+        if (lane == 0) got = mbar_wait(C::merge_empty(sb, part), mph ^ 1u, abort_flag);
         got = __shfl_sync(0xFFFFFFFFu, got, 0);
         if (!got) {
           if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
+          ok = false;
           break;
         }
 #pragma unroll
         for (int s = 0; s < MT; ++s) {
-          const int slot_m = ((part - 1) * MT + s) * kRowsPerSub + row_in_sub;
-          merge_val[slot_m] = best_val[s];
-          merge_idx[slot_m] = best_idx[s];
+          if (s == part) continue;
+          merge_val[(part * MT + s) * kRowsPerSub + row_in_sub] = best_val[s];
+          merge_idx[(part * MT + s) * kRowsPerSub + row_in_sub] = best_idx[s];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(C::merge_full(sb));
-        continue;
+        if (lane == 0) mbar_arrive(C::merge_full(sb, part));
       }
-      int got = 1;
-      if (lane == 0) got = mbar_wait(C::merge_full(sb), mph, abort_flag);
-      got = __shfl_sync(0xFFFFFFFFu, got, 0);
-      if (!got) {
-        if (lane == 0) raise_abort(abort_flag, err, kErrEpilogue);
-        break;
-      }
-#pragma unroll
-      for (int s = 0; s < MT; ++s) {
-#pragma unroll
-        for (int p = 1; p < kParts; ++p) {
-          const int slot_m = ((p - 1) * MT + s) * kRowsPerSub + row_in_sub;
-          const float v1 = merge_val[slot_m];
-          const int i1 = merge_idx[slot_m];
-          if (v1 > best_val[s] || (v1 == best_val[s] && i1 < best_idx[s])) {
-            best_val[s] = v1;
-            best_idx[s] = i1;
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(C::merge_empty(sb));
-      if (ch0 != 0 || ch1 != nchunks) {
-        // Part of a tile shared with other CTAs (split mode): its per-row best
-        // goes to the partials slot of this CTA's first or last segment.
-        const int slot = 2 * unit + (first_seg ? 0 : 1);
-#pragma unroll
-        for (int s = 0; s < MT; ++s) {
-          const size_t at =
-              static_cast<size_t>(slot) * rows_per_tile + s * kRowsPerSub + row_in_sub;
-          partial_val[at] = best_val[s];
-          partial_idx[at] = best_idx[s];
-        }
-        continue;
-      }
-#pragma unroll
-      for (int s = 0; s < MT; ++s) {
-        const int row = row0 + s * kRowsPerSub + row_in_sub;
-        const bool valid_row = row < N;
-        if (valid_row) ids[static_cast<size_t>(b) * N + row] = best_idx[s];
-        if (counts != nullptr) {
-          const uint32_t active = __ballot_sync(0xFFFFFFFFu, valid_row);
-          if (valid_row) {
-            const uint32_t peers = __match_any_sync(active, best_idx[s]);
-            if (lane == __ffs(peers) - 1)
-              atomicAdd(counts + static_cast<size_t>(b) * K + best_idx[s], __popc(peers));
-          }
-        }
+      if (owns) {
+        pend_tile = tile;
+        pend_val = part == 0 ? best_val[0] : best_val[MT - 1];
+        pend_idx = part == 0 ? best_idx[0] : best_idx[MT - 1];
+        // A tile shared with other CTAs (split mode) leaves its per-row best in
+        // the partials slot of this CTA's first or last segment.
+        pend_pslot = (ch0 != 0 || ch1 != nchunks) ? 2 * unit + (first_seg ? 0 : 1) : -1;
       }
     }
+    if (ok && pend_tile >= 0) finish();
   }
-
   // No remote signal may target a CTA that has exited: the pair leaves together.
   if constexpr (CG == 2)
     cluster_sync();
