@@ -100,13 +100,23 @@ struct Cfg {
   static constexpr int kCStageBytes = DB * kCBlockBytes;
   static constexpr int kAextSubBytes = kRowsPerSub * kExtBytes;
   static constexpr int kCextStageBytes = kNB * kExtBytes;
-  static constexpr int kOffX = 0;
-  static constexpr int kOffC = kOffX + MT * kXSubBytes;
-  static constexpr int kOffAext = kOffC + ST * kCStageBytes;
-  static constexpr int kOffCext = kOffAext + MT * kAextSubBytes;
-  static constexpr int kOffBar = kOffCext + ST * kCextStageBytes;
   // Accumulator slots: all 512 TMEM columns, NC columns each (2 or 4 slots).
   static constexpr int kSlots = 512 / NC;
+  // Shared memory of the whole layout with xs row-tile buffers.
+  static constexpr int layout_bytes(int xs) {
+    return xs * MT * (kXSubBytes + kAextSubBytes) + ST * (kCStageBytes + kCextStageBytes) +
+           (2 * xs * MT + 2 * ST + 2 * kSlots + 1 + 2 * kParts) * 8 + 16 +
+           kParts * MT * kRowsPerSub * 8 + 1024;
+  }
+  // Row-tile (x) buffers: two where they fit, so the next tile's x is loaded
+  // while the MMA still reads the current one (at D <= 64 a tile is only a few
+  // chunks long and a single buffer exposes the x load at every tile start).
+  static constexpr int kXS = layout_bytes(2) <= kSmemLimit ? 2 : 1;
+  static constexpr int kOffX = 0;
+  static constexpr int kOffC = kOffX + kXS * MT * kXSubBytes;
+  static constexpr int kOffAext = kOffC + ST * kCStageBytes;
+  static constexpr int kOffCext = kOffAext + kXS * MT * kAextSubBytes;
+  static constexpr int kOffBar = kOffCext + ST * kCextStageBytes;
   // Epilogue ownership: with two sub-tiles per tile, each half of the epilogue
   // warps can own one sub-tile (all NC columns of its items); otherwise the
   // halves split the columns of every item and exchange per-row bests. Owning
@@ -115,9 +125,10 @@ struct Cfg {
   // B200 it is faster for D <= 64 (c4 assign 123 -> 100 us) and slower at
   // D = 128 (c3 0.853 -> 0.902 ms), so it is used for short items only.
   static constexpr bool kOwn = MT == kParts && (DB == 1 || NC == 128);
-  // x_full[MT] x_empty[MT] c_full[ST] c_empty[ST] acc_full[kSlots]
-  // acc_empty[kSlots] drain merge_full[kParts] merge_empty[kParts]
-  static constexpr int kNumBars = 2 * MT + 2 * ST + 2 * kSlots + 1 + 2 * kParts;
+  // x_full[XM] x_empty[XM] c_full[ST] c_empty[ST] acc_full[kSlots]
+  // acc_empty[kSlots] drain merge_full[kParts] merge_empty[kParts], XM = kXS * MT
+  static constexpr int kXM = kXS * MT;
+  static constexpr int kNumBars = 2 * kXM + 2 * ST + 2 * kSlots + 1 + 2 * kParts;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   // per-row bests exchanged between column slices: (sender, sub) x 128 x (f32, i32)
   static constexpr int kOffMerge = kOffMisc + 16;
@@ -128,35 +139,39 @@ struct Cfg {
   static constexpr uint32_t kCTxBytes = CG * (kCStageBytes + kCextStageBytes);
   static constexpr uint32_t kTmemCols = kSlots * NC;
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget exceeded");
+  static_assert(kSmemBytes == layout_bytes(kXS), "layout size");
   static_assert(NC % 32 == 0 && NC >= 32 && NC <= 256, "UMMA N");
   static_assert(kNB % 16 == 0, "TMA box rows / UMMA N granularity");
   static_assert(NC == 128 || NC == 256, "accumulator slots tile the 512 TMEM columns");
   static_assert(kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
 
-  __device__ static uint32_t x_full(uint32_t base, int s) { return base + kOffBar + 8 * s; }
-  __device__ static uint32_t x_empty(uint32_t base, int s) { return base + kOffBar + 8 * (MT + s); }
+  // x buffer xi = (tile buffer) * MT + sub-tile
+  __device__ static uint32_t x_full(uint32_t base, int xi) { return base + kOffBar + 8 * xi; }
+  __device__ static uint32_t x_empty(uint32_t base, int xi) {
+    return base + kOffBar + 8 * (kXM + xi);
+  }
   __device__ static uint32_t c_full(uint32_t base, int st) {
-    return base + kOffBar + 8 * (2 * MT + st);
+    return base + kOffBar + 8 * (2 * kXM + st);
   }
   __device__ static uint32_t c_empty(uint32_t base, int st) {
-    return base + kOffBar + 8 * (2 * MT + ST + st);
+    return base + kOffBar + 8 * (2 * kXM + ST + st);
   }
   __device__ static uint32_t acc_full(uint32_t base, int a) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + a);
+    return base + kOffBar + 8 * (2 * kXM + 2 * ST + a);
   }
   __device__ static uint32_t acc_empty(uint32_t base, int a) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + kSlots + a);
+    return base + kOffBar + 8 * (2 * kXM + 2 * ST + kSlots + a);
   }
   __device__ static uint32_t drain(uint32_t base) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots);
+    return base + kOffBar + 8 * (2 * kXM + 2 * ST + 2 * kSlots);
   }
   // Bests sent by slice p are ready / have been consumed.
   __device__ static uint32_t merge_full(uint32_t base, int p) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots + 1 + p);
+    return base + kOffBar + 8 * (2 * kXM + 2 * ST + 2 * kSlots + 1 + p);
   }
   __device__ static uint32_t merge_empty(uint32_t base, int p) {
-    return base + kOffBar + 8 * (2 * MT + 2 * ST + 2 * kSlots + 1 + kParts + p);
+    return base + kOffBar + 8 * (2 * kXM + 2 * ST + 2 * kSlots + 1 + kParts + p);
   }
 };
 
@@ -399,9 +414,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int rows_per_tile = CG * MT * kRowsPerSub;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < MT; ++s) {
-      mbar_init(C::x_full(sb, s), 1);
-      mbar_init(C::x_empty(sb, s), 1);
+    for (int xi = 0; xi < C::kXM; ++xi) {
+      mbar_init(C::x_full(sb, xi), 1);
+      mbar_init(C::x_empty(sb, xi), 1);
     }
     for (int st = 0; st < ST; ++st) {
       mbar_init(C::c_full(sb, st), 1);
@@ -455,11 +470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- TMA
     uint32_t c_it = 0, x_it = 0;
     int c_last_ph[ST];
-    int x_last_ph[MT];
+    int x_last_ph[C::kXM];
 #pragma unroll
     for (int st = 0; st < ST; ++st) c_last_ph[st] = -1;
 #pragma unroll
-    for (int s = 0; s < MT; ++s) x_last_ph[s] = -1;
+    for (int xi = 0; xi < C::kXM; ++xi) x_last_ph[xi] = -1;
     bool ok = true;
     SegIter seg(split, nchunks, total_tiles, unit, units);
     int tile, ch0, ch1;
@@ -489,25 +504,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         c_last_ph[st] = static_cast<int>(ph);
         ++c_it;
         if (ch == ch0) {
+          const int xb = static_cast<int>(x_it % C::kXS);
+          const uint32_t xph = (x_it / C::kXS) & 1u;
 #pragma unroll
           for (int s = 0; s < MT; ++s) {
-            if (!warp_wait(C::x_empty(sb, s), (x_it & 1u) ^ 1u, abort_flag, lane)) {
+            const int xi = xb * MT + s;
+            if (!warp_wait(C::x_empty(sb, xi), xph ^ 1u, abort_flag, lane)) {
               if (lane == 0) raise_abort(abort_flag, err, kErrProducerX);
               ok = false;
               break;
             }
             if (lane == 0) {
-              if (leader) mbar_arrive_expect_tx(C::x_full(sb, s), C::kXTxBytes);
-              const uint32_t xfull = C::x_full(sb_lead, s);
+              if (leader) mbar_arrive_expect_tx(C::x_full(sb, xi), C::kXTxBytes);
+              const uint32_t xfull = C::x_full(sb_lead, xi);
 #pragma unroll
               for (int kb = 0; kb < DB; ++kb)
-                tma_load<CG>(sb + C::kOffX + (s * DB + kb) * (kRowsPerSub * kKBlockBytes), &tm_x,
+                tma_load<CG>(sb + C::kOffX + (xi * DB + kb) * (kRowsPerSub * kKBlockBytes), &tm_x,
                              xfull, kb * kKBlockElems, row0 + s * kRowsPerSub, b);
-              tma_load<CG>(sb + C::kOffAext + s * C::kAextSubBytes, &tm_aext, xfull, 0,
+              tma_load<CG>(sb + C::kOffAext + xi * C::kAextSubBytes, &tm_aext, xfull, 0,
                            row0 + s * kRowsPerSub, b);
             }
             __syncwarp();
-            x_last_ph[s] = static_cast<int>(x_it & 1u);
+            x_last_ph[xi] = static_cast<int>(xph);
           }
         }
       }
@@ -522,9 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait(C::c_full(sb, st), static_cast<uint32_t>(c_last_ph[st]), abort_flag,
                     100000000ull);
 #pragma unroll
-      for (int s = 0; s < MT; ++s)
-        if (x_last_ph[s] >= 0)
-          mbar_wait(C::x_full(sb, s), static_cast<uint32_t>(x_last_ph[s]), abort_flag,
+      for (int xi = 0; xi < C::kXM; ++xi)
+        if (x_last_ph[xi] >= 0)
+          mbar_wait(C::x_full(sb, xi), static_cast<uint32_t>(x_last_ph[xi]), abort_flag,
                     100000000ull);
     }
   } else if (warp == 1) {
@@ -550,7 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t c_stage = sb + C::kOffC + st * C::kCStageBytes;
 #pragma unroll
           for (int s = 0; s < MT; ++s) {
-            if (ch == ch0 && !mbar_wait(C::x_full(sb, s), x_it & 1u, abort_flag)) {
+            const int xi = static_cast<int>(x_it % C::kXS) * MT + s;
+            if (ch == ch0 && !mbar_wait(C::x_full(sb, xi), (x_it / C::kXS) & 1u, abort_flag)) {
               raise_abort(abort_flag, err, kErrMmaX);
               ok = false;
               break;
@@ -567,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // with two epilogue warps, and every issue slot it needs is one
             // they compete for (measured: the MMA stream slows by the
             // epilogue work of this sub-partition alone).
-            const uint32_t a_lo = umma_desc_lo(sb + C::kOffX + s * C::kXSubBytes);
+            const uint32_t a_lo = umma_desc_lo(sb + C::kOffX + xi * C::kXSubBytes);
             const uint32_t b_lo = umma_desc_lo(c_stage);
 #pragma unroll
             for (int ks = 0; ks < DB * 4; ++ks) {
@@ -586,11 +605,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         idesc, accf);
               }
             }
-            mma<CG>(d_tmem, umma_desc(umma_desc_lo(sb + C::kOffAext + s * C::kAextSubBytes), kHi32),
+            mma<CG>(d_tmem, umma_desc(umma_desc_lo(sb + C::kOffAext + xi * C::kAextSubBytes), kHi32),
                     umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
                     idesc_ext, 1u);
             mma_done<CG>(C::acc_full(sb, slot));
-            if (ch == ch1 - 1) mma_done<CG>(C::x_empty(sb, s));
+            if (ch == ch1 - 1) mma_done<CG>(C::x_empty(sb, xi));
             ++item;
           }
           mma_done<CG>(C::c_empty(sb, st));
@@ -1039,7 +1058,7 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
     if (D <= 192) return FKC_TC(3, 2, 256, 2, 2);
     return FKC_TC(4, 1, 256, 2, 2);
   } else {
-    if (D <= 64) return FKC_TC(1, 2, 256, 4, 1);
+    if (D <= 64) return FKC_TC(1, 2, 256, 3, 1);  // two x tile buffers fit
     if (D <= 128) return FKC_TC(2, 2, 256, 2, 1);
     if (D <= 192) return FKC_TC(3, 2, 128, 2, 1);
     return FKC_TC(4, 1, 128, 2, 1);
