@@ -121,6 +121,31 @@ int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids
                           float* sums, int32_t* counts, int64_t B, int64_t N, int64_t K,
                           int64_t D, int dtype, cudaStream_t stream);
 
+// Fused update + finalize of the single-GPU Lloyd step (update.cu): clusters
+// of more than 64 rows are cut into units that add into a per-cluster row of
+// acc; the last unit of the cluster finishes it. done and acc are zero between
+// passes (zero_bytes from done on are zeroed when the workspace is prepared).
+struct UpdatePlan {
+  int2* extras;          // (B, cap) (cluster b*K+k, chunk) of the split clusters' units
+  int32_t* extra_count;  // (B) entries used in each row of extras
+  int32_t* done;         // (B, K) finished units of each split cluster
+  float* acc;            // (B, K, D) sums of split clusters being accumulated
+  int cap;
+  size_t zero_bytes;     // done .. end of acc
+};
+size_t update_plan_bytes(int64_t B, int64_t N, int64_t K, int64_t D);
+UpdatePlan carve_update_plan(void* ws, int64_t B, int64_t N, int64_t K, int64_t D);
+// Rows of whole 16-byte vectors (at most 32 per row) and 16-byte aligned buffers.
+bool fused_update_ok(const void* x, const void* old_c, const void* new_c, const float* sums,
+                     int64_t D, int dtype);
+// counts: the histogram of ids (labels all in [0,K)). Writes sums, new_c,
+// c_sq/cext (nullable) of new_c and shift (nullable) = max ||new - old||.
+int launch_update_finalize(const void* x, const int32_t* ids, const int32_t* counts,
+                           const UpdateWorkspace& w, const UpdatePlan& plan, const void* old_c,
+                           void* new_c, float* sums, float* c_sq, void* cext, float* shift,
+                           int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                           cudaStream_t stream);
+
 // Whole-loop CUDA graph (lloyd_graph.cu).
 struct LoopCtl {
   int32_t iter;       // iterations completed in the current launch

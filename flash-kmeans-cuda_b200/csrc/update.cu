@@ -68,22 +68,55 @@ __global__ void histogram_kernel(const int32_t* __restrict__ ids, int32_t* __res
 
 // Exclusive scan of counts[b, 0..K) into offsets[b, 0..K) and cursor[b, 0..K);
 // one CTA of kScanThreads per b, V consecutive counts per thread per tile
-// (V = 4 with 16-byte loads and stores when K % 4 == 0).
+// (V = 4 with 16-byte loads and stores when K % 4 == 0). With PLAN it also
+// lays out the units of the fused update (clusters of more than kUnitRows
+// rows: ceil(count / kUnitRows) units each, listed in extras[b, 0..cap) in
+// cluster order).
 constexpr int kScanThreads = 1024;
+constexpr int kUnitRows = 64;  // rows of x summed by one unit of the fused update
 
-template <int V>
-__global__ void __launch_bounds__(kScanThreads) scan_kernel(const int32_t* __restrict__ counts,
-                                                            int32_t* __restrict__ offsets,
-                                                            int32_t* __restrict__ cursor, int K) {
-  pdl_wait();
-  __shared__ int warp_tot[kScanThreads / 32];
-  __shared__ int carry_s;
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const int32_t* cnt = counts + static_cast<size_t>(blockIdx.x) * K;
-  int32_t* off = offsets + static_cast<size_t>(blockIdx.x) * K;
-  int32_t* cur = cursor + static_cast<size_t>(blockIdx.x) * K;
-  if (t == 0) carry_s = 0;
+// Exclusive scan over the CTA (every thread gets the CTA total too). Ends with
+// a barrier, so warp_tot can be reused at once.
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_tot, int& total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) warp_tot[w] = inc;
   __syncthreads();
+  if (w == 0) {
+    int t = warp_tot[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xFFFFFFFFu, t, o);
+      if (lane >= o) t += u;
+    }
+    warp_tot[lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  const int excl = inc - v + (w > 0 ? warp_tot[w - 1] : 0);
+  total = warp_tot[kScanThreads / 32 - 1];
+  __syncthreads();
+  return excl;
+}
+
+template <int V, bool PLAN>
+__global__ void __launch_bounds__(kScanThreads) scan_kernel(
+    const int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+    int32_t* __restrict__ cursor, int K, int2* __restrict__ extras,
+    int32_t* __restrict__ extra_count, int cap) {
+  pdl_wait();
+  static_assert(kScanThreads == 1024, "block_excl_scan assumes 32 warps");
+  __shared__ int warp_tot[kScanThreads / 32];
+  const int t = threadIdx.x;
+  const size_t kb = static_cast<size_t>(blockIdx.x) * K;
+  const int32_t* cnt = counts + kb;
+  int32_t* off = offsets + kb;
+  int32_t* cur = cursor + kb;
+  int carry = 0, xcarry = 0;
   for (int t0 = 0; t0 < K; t0 += kScanThreads * V) {
     const int i0 = t0 + t * V;
     int c[V];
@@ -101,26 +134,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int32_t* __res
     int local = 0;
 #pragma unroll
     for (int e = 0; e < V; ++e) local += c[e];
-    int v = local;  // inclusive warp scan of the per-thread sums
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xFFFFFFFFu, v, o);
-      if (lane >= o) v += u;
-    }
-    if (lane == 31) warp_tot[w] = v;
-    __syncthreads();
-    if (w == 0) {
-      int s = warp_tot[lane];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xFFFFFFFFu, s, o);
-        if (lane >= o) s += u;
-      }
-      warp_tot[lane] = s;  // inclusive over warps
-    }
-    __syncthreads();
-    const int carry = carry_s;
-    int run = carry + v - local + (w > 0 ? warp_tot[w - 1] : 0);
+    int total = 0;
+    int run = carry + block_excl_scan(local, warp_tot, total);
+    carry += total;
     int o[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) {
@@ -137,10 +153,27 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(const int32_t* __res
       for (int e = 0; e < V; ++e)
         if (i0 + e < K) off[i0 + e] = cur[i0 + e] = o[e];
     }
-    __syncthreads();  // everyone has read carry_s and warp_tot
-    if (t == kScanThreads - 1) carry_s = run;
-    __syncthreads();
+    if constexpr (PLAN) {
+      int ux[V], lx = 0;
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        ux[e] = c[e] > kUnitRows ? (c[e] + kUnitRows - 1) / kUnitRows : 0;
+        lx += ux[e];
+      }
+      int xtotal = 0;
+      int xrun = xcarry + block_excl_scan(lx, warp_tot, xtotal);
+      xcarry += xtotal;
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        if (ux[e] == 0) continue;
+        const int kg = static_cast<int>(kb) + i0 + e;
+        int2* dst = extras + static_cast<size_t>(blockIdx.x) * cap + xrun;
+        for (int j = 0; j < ux[e]; ++j) dst[j] = make_int2(kg, j);
+        xrun += ux[e];
+      }
+    }
   }
+  if (PLAN && t == 0) extra_count[blockIdx.x] = xcarry;
 }
 
 // Chunked scatter (K <= kLocalMaxK): the CTA ranks its rows per cluster with
@@ -194,7 +227,7 @@ __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
     const int pos = cnt[id[i]] + lr[i];
     if (pos >= N) continue;  // counts inconsistent with ids: drop rather than overrun
     perm[rb + pos] = r0 + i * kSortThreads + t;
-    ids_sorted[rb + pos] = id[i];
+    if (ids_sorted != nullptr) ids_sorted[rb + pos] = id[i];
   }
 }
 
@@ -232,7 +265,7 @@ __global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
       if (pos < N) {  // counts inconsistent with ids: drop rather than overrun
         const int64_t dst = b * N + pos;
         perm[dst] = static_cast<int32_t>(i - b * N);
-        ids_sorted[dst] = id;
+        if (ids_sorted != nullptr) ids_sorted[dst] = id;
       }
     }
   }
@@ -392,6 +425,165 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
       }
     }
     flush();
+  }
+}
+
+// Fused update + finalize (single-GPU Lloyd step). Work units: unit b*K+k is
+// cluster k of batch row b when it has at most kUnitRows rows; larger clusters
+// are cut into units of kUnitRows rows listed in extras (scan_kernel<.., true>).
+// A group of L lanes (lane i: 16-byte vector i of a row) takes a unit, reads
+// its rows through perm with P loads in flight (the next P row indices are
+// fetched while the rows arrive) and sums them in registers in row order.
+// A whole cluster is finished at once: sums row (plain stores), new centroid
+// = sums / count rounded to T (the old one when empty), ||new||^2, its norm
+// slice and ||new - old|| for the shift, so no sums zero-fill, no atomics on
+// sums and no separate finalize pass are needed. A unit of a split cluster
+// adds its partial sum into the cluster's row of `acc` (16-byte vector
+// atomics); the last one to finish (done counter) reads the row, finishes the
+// cluster and sets the row and the counter back to zero, so both stay zero
+// between passes (they are zeroed once, when the workspace is prepared).
+// new_c may alias old_c: each lane reads its old elements before writing.
+template <typename T, int L, int P>
+__global__ void __launch_bounds__(256) gather_finalize_kernel(
+    const T* __restrict__ x, const int32_t* __restrict__ perm,
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ counts,
+    const int2* __restrict__ extras, const int32_t* __restrict__ extra_count,
+    int32_t* __restrict__ done, float* __restrict__ acc_rows, const T* old_c, T* new_c,
+    float* __restrict__ sums, float* __restrict__ c_sq_out, uint8_t* __restrict__ cext_out,
+    float* __restrict__ shift_out, int N, int K, int B, int cap) {
+  pdl_wait();
+  constexpr int kVec = 16 / sizeof(T);
+  constexpr int G = 32 / L;
+  static_assert(32 % L == 0, "groups tile the warp");
+  const int lane = threadIdx.x & 31;
+  const int g = lane / L;
+  const int i = lane % L;
+  const uint32_t gmask = L == 32 ? 0xFFFFFFFFu : (((1u << L) - 1u) << (g * L));
+  const int D = L * kVec;
+  const int64_t BK = static_cast<int64_t>(B) * K;
+  const int64_t U = BK + static_cast<int64_t>(B) * cap;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  float shift_max = 0.f;
+  for (int64_t u0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * G;
+       u0 < U; u0 += warps * G) {
+    const int64_t u = u0 + g;
+    int kg = -1, cnt = 0, r0 = 0, r1 = 0, nunits = 1;
+    int64_t e = -1;
+    if (u < BK) {
+      cnt = counts[u];
+      if (cnt <= kUnitRows) {
+        kg = static_cast<int>(u);
+        r0 = offsets[u];
+        r1 = r0 + cnt;
+      }
+    } else if (u < U) {
+      const int64_t q = u - BK;
+      const int b = static_cast<int>(q / cap);
+      if (q - static_cast<int64_t>(b) * cap < extra_count[b]) {
+        const int2 en = extras[q];
+        kg = en.x;
+        e = q;
+        cnt = counts[kg];
+        nunits = (cnt + kUnitRows - 1) / kUnitRows;
+        r0 = offsets[kg] + en.y * kUnitRows;
+        r1 = min(r0 + kUnitRows, offsets[kg] + cnt);
+      }
+    }
+    float acc[kVec];
+#pragma unroll
+    for (int v = 0; v < kVec; ++v) acc[v] = 0.f;
+    if (kg >= 0) {
+      const int b = kg / K;
+      const int32_t* pb = perm + static_cast<size_t>(b) * N;
+      const T* xb = x + static_cast<size_t>(b) * N * D + i * kVec;
+      int pr[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) pr[p] = r0 + p < r1 ? pb[r0 + p] : 0;
+      for (int r = r0; r < r1; r += P) {
+        uint4 v[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+          if (r + p < r1) v[p] = ld_stream_v4(xb + static_cast<size_t>(pr[p]) * D);
+#pragma unroll
+        for (int p = 0; p < P; ++p) pr[p] = r + P + p < r1 ? pb[r + P + p] : 0;
+#pragma unroll
+        for (int p = 0; p < P; ++p)
+          if (r + p < r1) add_vec<T>(acc, v[p]);
+      }
+      if (e >= 0) {
+        // A unit of a split cluster: add the partial, count it, and let the
+        // last unit of the cluster finish it.
+        float* arow = acc_rows + static_cast<size_t>(kg) * D + i * kVec;
+#pragma unroll
+        for (int v = 0; v < kVec; v += 4) red_add_v4(arow + v, acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
+        __threadfence();
+        __syncwarp(gmask);
+        int prev = 0;
+        if (i == 0) prev = atomicAdd(done + kg, 1);
+        prev = __shfl_sync(gmask, prev, g * L);
+        if (prev != nunits - 1) {
+          kg = -1;
+        } else {
+          __threadfence();
+#pragma unroll
+          for (int v = 0; v < kVec; v += 4) {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(arow + v));
+            acc[v] = f.x;
+            acc[v + 1] = f.y;
+            acc[v + 2] = f.z;
+            acc[v + 3] = f.w;
+            *reinterpret_cast<float4*>(arow + v) = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          if (i == 0) done[kg] = 0;
+        }
+      }
+    }
+    if (kg >= 0) {
+      const size_t row = static_cast<size_t>(kg) * D + i * kVec;
+      float* srow = sums + row;
+#pragma unroll
+      for (int v = 0; v < kVec; v += 4)
+        *reinterpret_cast<float4*>(srow + v) = make_float4(acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
+      const uint4 ov = *reinterpret_cast<const uint4*>(old_c + row);
+      const T* o = reinterpret_cast<const T*>(&ov);
+      uint4 nvv;
+      T* nv = reinterpret_cast<T*>(&nvv);
+      const float fc = static_cast<float>(cnt);
+      float sq = 0.f, sh = 0.f;
+#pragma unroll
+      for (int v = 0; v < kVec; ++v) {
+        nv[v] = cnt > 0 ? from_f32<T>(__fdiv_rn(acc[v], fc)) : o[v];
+        const float nf = to_f32<T>(nv[v]);
+        const float df = nf - to_f32<T>(o[v]);
+        sq = fmaf(nf, nf, sq);
+        sh = fmaf(df, df, sh);
+      }
+      *reinterpret_cast<uint4*>(new_c + row) = nvv;
+#pragma unroll
+      for (int o2 = L / 2; o2 >= 1; o2 >>= 1) {
+        sq += __shfl_xor_sync(gmask, sq, o2);
+        sh += __shfl_xor_sync(gmask, sh, o2);
+      }
+      if (i == 0) {
+        if (c_sq_out != nullptr) c_sq_out[kg] = sq;
+        if (cext_out != nullptr)
+          write_norm_ext(cext_out + static_cast<size_t>(kg) * kNormExtBytes, -0.5f * sq, false);
+        shift_max = fmaxf(shift_max, sqrtf(sh));
+      }
+    }
+  }
+  if (shift_out != nullptr) {
+    __shared__ float block_max[8];
+#pragma unroll
+    for (int o2 = 16; o2 >= 1; o2 >>= 1)
+      shift_max = fmaxf(shift_max, __shfl_xor_sync(0xFFFFFFFFu, shift_max, o2));
+    if (lane == 0) block_max[threadIdx.x >> 5] = shift_max;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float m = 0.f;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) m = fmaxf(m, block_max[w]);
+      atomicMax(reinterpret_cast<unsigned int*>(shift_out), __float_as_uint(m));
+    }
   }
 }
 
@@ -670,20 +862,11 @@ int launch_scatter_chunk(const int32_t* ids, const UpdateWorkspace& w, int64_t B
 
 }  // namespace
 
-int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
-                         int64_t B, int64_t N, int64_t K, bool all_valid, cudaStream_t stream) {
-  FKC_REQUIRE(B <= 2147483647ll && N <= 2147483647ll && K <= 2147483647ll,
-              "update: sizes out of range");
-  if (K % 4 == 0)
-    FKC_TRY(launch_pdl(scan_kernel<4>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads), 0,
-                       stream, counts, w.offsets, w.cursor, static_cast<int>(K)));
-  else
-    FKC_TRY(launch_pdl(scan_kernel<1>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads), 0,
-                       stream, counts, w.offsets, w.cursor, static_cast<int>(K)));
-  // With labels outside [0,K) some sorted positions stay unwritten: they must
-  // read as label -1, which the accumulator skips.
-  if (!all_valid)
-    FKC_CUDA_TRY(cudaMemsetAsync(w.ids_sorted, 0xFF, static_cast<size_t>(B * N) * 4, stream));
+namespace {
+
+// perm (and ids_sorted, when non-null) from the cursors of the scan.
+int launch_scatter(const int32_t* ids, const UpdateWorkspace& w, int64_t B, int64_t N, int64_t K,
+                   cudaStream_t stream) {
   if (K <= kLocalMaxK) {
     // Rows per chunk: the largest of 4096/2048/1024/512 that still gives about
     // two chunks per SM.
@@ -699,6 +882,27 @@ int launch_counting_sort(const int32_t* ids, const int32_t* counts, const Update
                     w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K));
 }
 
+}  // namespace
+
+int launch_counting_sort(const int32_t* ids, const int32_t* counts, const UpdateWorkspace& w,
+                         int64_t B, int64_t N, int64_t K, bool all_valid, cudaStream_t stream) {
+  FKC_REQUIRE(B <= 2147483647ll && N <= 2147483647ll && K <= 2147483647ll,
+              "update: sizes out of range");
+  if (K % 4 == 0)
+    FKC_TRY(launch_pdl(scan_kernel<4, false>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads),
+                       0, stream, counts, w.offsets, w.cursor, static_cast<int>(K), nullptr,
+                       nullptr, 0));
+  else
+    FKC_TRY(launch_pdl(scan_kernel<1, false>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads),
+                       0, stream, counts, w.offsets, w.cursor, static_cast<int>(K), nullptr,
+                       nullptr, 0));
+  // With labels outside [0,K) some sorted positions stay unwritten: they must
+  // read as label -1, which the accumulator skips.
+  if (!all_valid)
+    FKC_CUDA_TRY(cudaMemsetAsync(w.ids_sorted, 0xFF, static_cast<size_t>(B * N) * 4, stream));
+  return launch_scatter(ids, w, B, N, K, stream);
+}
+
 int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids_sorted,
                           float* sums, int32_t* counts, int64_t B, int64_t N, int64_t K,
                           int64_t D, int dtype, cudaStream_t stream) {
@@ -710,6 +914,131 @@ int launch_run_accumulate(const void* x, const int32_t* perm, const int32_t* ids
                                                  stream);
     case FKC_DTYPE_F32:
       return run_accumulate_typed<float>(x, perm, ids_sorted, sums, counts, B, N, K, D, stream);
+    default:
+      return set_error(FKC_EINVAL, "update: bad dtype %d", dtype);
+  }
+}
+
+namespace {
+
+int64_t plan_cap(int64_t N) {
+  // Units of split clusters in one batch row: sum of ceil(c / kUnitRows) over
+  // clusters with c > kUnitRows <= N / kUnitRows + (number of such clusters)
+  // <= 2 N / kUnitRows.
+  return 2 * ((N + kUnitRows - 1) / kUnitRows);
+}
+
+template <typename T, int L>
+int launch_gather_finalize(const T* x, const UpdateWorkspace& w, const UpdatePlan& plan,
+                           const int32_t* counts, const T* old_c, T* new_c, float* sums,
+                           float* c_sq, void* cext, float* shift, int64_t B, int64_t N,
+                           int64_t K, cudaStream_t stream) {
+  constexpr int P = L >= 16 ? 16 : 8;  // row loads in flight per group
+  auto kern = gather_finalize_kernel<T, L, P>;
+  static int cap = 0;  // resident blocks; the same on every device of one model
+  if (cap == 0) cap = resident_blocks(kern);
+  constexpr int G = 32 / L;
+  const int64_t units = B * K + B * static_cast<int64_t>(plan.cap);
+  const int64_t blocks = std::min<int64_t>((units + 8 * G - 1) / (8 * G), cap);
+  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, w.perm,
+                    w.offsets, counts, plan.extras, plan.extra_count, plan.done, plan.acc,
+                    old_c, new_c, sums, c_sq, static_cast<uint8_t*>(cext), shift,
+                    static_cast<int>(N), static_cast<int>(K), static_cast<int>(B), plan.cap);
+}
+
+template <typename T>
+int update_finalize_typed(const void* x, const UpdateWorkspace& w, const UpdatePlan& plan,
+                          const int32_t* counts, const void* old_c, void* new_c, float* sums,
+                          float* c_sq, void* cext, float* shift, int64_t B, int64_t N, int64_t K,
+                          int64_t D, cudaStream_t stream) {
+  const T* xt = static_cast<const T*>(x);
+  const T* oc = static_cast<const T*>(old_c);
+  T* nc = static_cast<T*>(new_c);
+  switch (static_cast<int>(D * sizeof(T) / 16)) {
+#define FKC_GF(L_)                                                                           \
+  case L_:                                                                                   \
+    return launch_gather_finalize<T, L_>(xt, w, plan, counts, oc, nc, sums, c_sq, cext, shift, \
+                                         B, N, K, stream);
+    FKC_GF(1)
+    FKC_GF(2)
+    FKC_GF(4)
+    FKC_GF(8)
+    FKC_GF(16)
+    FKC_GF(32)
+#undef FKC_GF
+    default:
+      return set_error(FKC_EINVAL, "fused update: unsupported row size (D=%lld)",
+                       static_cast<long long>(D));
+  }
+}
+
+}  // namespace
+
+size_t update_plan_bytes(int64_t B, int64_t N, int64_t K, int64_t D) {
+  const int64_t cap = plan_cap(N);
+  return align_up(static_cast<size_t>(B * cap) * 8, 256) + align_up(static_cast<size_t>(B) * 4, 256) +
+         align_up(static_cast<size_t>(B * K) * 4, 256) +
+         align_up(static_cast<size_t>(B * K * D) * 4, 256);
+}
+
+UpdatePlan carve_update_plan(void* ws, int64_t B, int64_t N, int64_t K, int64_t D) {
+  const int64_t cap = plan_cap(N);
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  UpdatePlan u;
+  u.extras = reinterpret_cast<int2*>(p);
+  p += align_up(static_cast<size_t>(B * cap) * 8, 256);
+  u.extra_count = reinterpret_cast<int32_t*>(p);
+  p += align_up(static_cast<size_t>(B) * 4, 256);
+  u.done = reinterpret_cast<int32_t*>(p);
+  p += align_up(static_cast<size_t>(B * K) * 4, 256);
+  u.acc = reinterpret_cast<float*>(p);
+  u.cap = static_cast<int>(cap);
+  u.zero_bytes = static_cast<size_t>(p - reinterpret_cast<uint8_t*>(u.done)) +
+                 static_cast<size_t>(B * K * D) * 4;
+  return u;
+}
+
+bool fused_update_ok(const void* x, const void* old_c, const void* new_c, const float* sums,
+                     int64_t D, int dtype) {
+  const int64_t es = dtype == FKC_DTYPE_F32 ? 4 : 2;
+  const int64_t row = D * es;
+  if (row % 16 != 0 || row > 512) return false;
+  const int64_t L = row / 16;
+  if (32 % L != 0) return false;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return al(x) && al(old_c) && al(new_c) && al(sums);
+}
+
+int launch_update_finalize(const void* x, const int32_t* ids, const int32_t* counts,
+                           const UpdateWorkspace& w, const UpdatePlan& plan, const void* old_c,
+                           void* new_c, float* sums, float* c_sq, void* cext, float* shift,
+                           int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                           cudaStream_t stream) {
+  FKC_REQUIRE(B <= 2147483647ll && N <= 2147483647ll && K <= 2147483647ll &&
+                  B * K <= 2147483647ll,
+              "update: sizes out of range");
+  if (K % 4 == 0)
+    FKC_TRY(launch_pdl(scan_kernel<4, true>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads),
+                       0, stream, counts, w.offsets, w.cursor, static_cast<int>(K), plan.extras,
+                       plan.extra_count, plan.cap));
+  else
+    FKC_TRY(launch_pdl(scan_kernel<1, true>, dim3(static_cast<unsigned>(B)), dim3(kScanThreads),
+                       0, stream, counts, w.offsets, w.cursor, static_cast<int>(K), plan.extras,
+                       plan.extra_count, plan.cap));
+  UpdateWorkspace ws = w;
+  ws.ids_sorted = nullptr;  // the fused pass walks clusters through offsets
+  FKC_TRY(launch_scatter(ids, ws, B, N, K, stream));
+  if (shift != nullptr) FKC_TRY(launch_zero_fill(shift, sizeof(float), stream));
+  switch (dtype) {
+    case FKC_DTYPE_F16:
+      return update_finalize_typed<__half>(x, w, plan, counts, old_c, new_c, sums, c_sq, cext,
+                                           shift, B, N, K, D, stream);
+    case FKC_DTYPE_BF16:
+      return update_finalize_typed<__nv_bfloat16>(x, w, plan, counts, old_c, new_c, sums, c_sq,
+                                                  cext, shift, B, N, K, D, stream);
+    case FKC_DTYPE_F32:
+      return update_finalize_typed<float>(x, w, plan, counts, old_c, new_c, sums, c_sq, cext,
+                                          shift, B, N, K, D, stream);
     default:
       return set_error(FKC_EINVAL, "update: bad dtype %d", dtype);
   }

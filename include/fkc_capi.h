@@ -168,7 +168,9 @@ FKC_CAPI_EXPORT int fkc_finalize(const float* sums, const int32_t* counts, const
 /* ------------------------------------------------------------------------
  * Lloyd iteration (kmeans.py:73-105 as device-resident steps). One workspace
  * of fkc_lloyd_workspace_size() bytes carries state between the calls:
- *   fkc_lloyd_prepare   once per x: per-row terms of the assignment.
+ *   fkc_lloyd_prepare   once per x: per-row terms of the assignment; also
+ *                       zeroes the fused update's accumulators (call it
+ *                       again after a failed fkc_lloyd_iter).
  *   fkc_lloyd_assign    labels ids (B,N) and per-cluster counts (B,K) (the
  *                       histogram is fused into the assignment kernel);
  *   fkc_lloyd_update    sums (B,K,D) fp32 from x, ids and those counts;
@@ -177,7 +179,10 @@ FKC_CAPI_EXPORT int fkc_finalize(const float* sums, const int32_t* counts, const
  *   fkc_lloyd_finalize  new centroids (+ shift_out if non-NULL) from the
  *                       (reduced) sums/counts; also prepares the next
  *                       iteration's centroid terms inside the workspace.
- *   fkc_lloyd_iter      local + finalize.
+ *   fkc_lloyd_iter      local + finalize. On one GPU (rows of whole 16-byte
+ *                       vectors, 16-byte aligned buffers) the update and the
+ *                       finalize run as one pass over the clusters; sums and
+ *                       counts are written all the same.
  * The centroids passed to fkc_lloyd_local must be those last produced by
  * fkc_lloyd_finalize with the same workspace, or fkc_lloyd_set_centroids
  * must be called first (initial centroids).

@@ -42,6 +42,9 @@ def _close_centroids(got, ref, dtype, rel=1e-3):
     (2, 10000, 700, 64, 0.0),
     (1, 9000, 2000, 128, 1.1),
     (1, 6000, 300, 384, 0.0),  # D > 256 (CTA pairs)
+    # small clusters on average (the fused update + finalize pass) with a few
+    # hot ones split into 64-row units that the cluster's last unit finishes
+    (2, 20000, 700, 64, 1.1),
 ])
 def test_teacher_forced_iterations(cuda_device, dtype, B, N, K, D, zipf):
     from flash_kmeans_cuda.kmeans import LloydState
@@ -65,10 +68,57 @@ def test_teacher_forced_iterations(cuda_device, dtype, B, N, K, D, zipf):
         counts = st.counts.cpu().numpy()
         s_ref, c_ref = orc.update(xn, ids, K)
         assert np.array_equal(counts, c_ref), f"iter {it}: counts"
+        # fp32 sums against float64, relative to the sum of magnitudes
+        s_abs, _ = orc.update(np.abs(xn), ids, K)
+        s_err = np.abs(st.sums.cpu().numpy() - s_ref)
+        assert (s_err <= 1e-5 * s_abs + 1e-6).all(), f"iter {it}: sums off by {s_err.max()}"
         fin = orc.finalize(s_ref, c_ref, cn, dtype)
         _close_centroids(to_np(nxt), fin, dtype)
         assert abs(st.shift.item() - orc.shift(to_np(nxt), cn)) <= 1e-3 * orc.shift(fin, cn) + 1e-3
         cur = nxt
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+def test_step_empty_and_split_clusters(cuda_device, dtype):
+    """One Lloyd step of the fused update + finalize pass (20 rows per cluster on
+    average) where all but 10 centroids are far from every point: 990 empty
+    clusters keep their centroid and the 10 others hold about 2000 rows each
+    (split into units). Sums, counts, centroids, norms and shift against the
+    oracle."""
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    B, N, K, D = 2, 20000, 1000, 128
+    x = mixture(B, N, D, 10, seed=71, dtype=dtype)
+    c = subset_init(x, K, seed=72).float()
+    c[:, 10:] += 50.0
+    c = c.to(x.dtype)
+    xd = x.cuda()
+    st = LloydState(xd, K)
+    cur = c.cuda()
+    st.set_centroids(cur)
+    nxt = torch.empty_like(cur)
+    st.step(cur, nxt, True)
+    torch.cuda.synchronize()
+    xn, cn = to_np(x), to_np(c)
+    ids = st.ids.cpu().numpy()
+    ref = orc.assign(xn, cn)
+    assert not ((ids != ref.ids) & ref.gap_mask()).any()
+    s_ref, c_ref = orc.update(xn, ids, K)
+    counts = st.counts.cpu().numpy()
+    assert np.array_equal(counts, c_ref)
+    assert (counts[:, 10:] == 0).all() and counts.max() > 1000
+    s_abs, _ = orc.update(np.abs(xn), ids, K)
+    assert (np.abs(st.sums.cpu().numpy() - s_ref) <= 1e-5 * s_abs + 1e-6).all()
+    fin = orc.finalize(s_ref, c_ref, cn, dtype)
+    got = to_np(nxt)
+    _close_centroids(got, fin, dtype)
+    assert np.array_equal(got[:, 10:], cn[:, 10:])  # empty clusters keep the old centroid
+    assert abs(st.shift.item() - orc.shift(got, cn)) <= 1e-3 * orc.shift(fin, cn) + 1e-3
+    # the next assignment uses the norms written with the new centroids
+    st.step(nxt, cur, False)
+    torch.cuda.synchronize()
+    ref2 = orc.assign(xn, got)
+    assert not ((st.ids.cpu().numpy() != ref2.ids) & ref2.gap_mask()).any()
 
 
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
