@@ -81,7 +81,10 @@ extern "C" FKC_CAPI_EXPORT int fkc_assign_noalloc(const void* x, const void* cen
   // The size check comes before any CUDA call. Shapes that do not take the
   // tensor-core path need no scratch (0 here); invalid shapes also give 0 and
   // are reported by fkc_assign's own argument checks.
-  const size_t need = fkc_assign_workspace_size(B, N, K, D, dtype);
+  size_t need = fkc_assign_workspace_size(B, N, K, D, dtype);
+  // fp32 beyond the scratch: the CUDA-core kernel, which needs no scratch.
+  if (dtype == FKC_DTYPE_F32 && need > static_cast<size_t>(FKC_ASSIGN_NOALLOC_SCRATCH_BYTES))
+    need = 0;
   if (need > static_cast<size_t>(FKC_ASSIGN_NOALLOC_SCRATCH_BYTES))
     return fkc::set_error(
         FKC_EWORKSPACE,

@@ -135,18 +135,34 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 
 namespace {
 
+// fp32 inputs on the tensor cores: x and the centroids are split into bf16
+// hi/lo rows of 3D elements (hi.hi + hi.lo + lo.hi, see launch_split_bf16), so
+// 3D must fit the bf16 kernel (D <= 128).
+bool split_f32(int64_t D, int dtype) {
+  return dtype == FKC_DTYPE_F32 && D >= 16 && D <= 128 && D % 16 == 0;
+}
+
 // Shape/dtype eligibility of the tensor-core assignment, independent of the
 // device (workspace sizes must not depend on which GPU is current).
 bool tc_shape_ok(int64_t D, int dtype) {
-  return (dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 384 &&
-         D % 16 == 0;
+  return ((dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 384 &&
+          D % 16 == 0) ||
+         split_f32(D, dtype);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool use_tc(const void* x, const void* c, int64_t D, int dtype) {
+  const bool split = split_f32(D, dtype);
   return tc_shape_ok(D, dtype) && !force_safe_path() && aligned16(x) && aligned16(c) &&
-         assign_tc_supported(D, dtype);
+         assign_tc_supported(split ? 3 * D : D, split ? FKC_DTYPE_BF16 : dtype);
+}
+
+// Operand rows of the split-fp32 path: x3 (B, N, 3D) and c3 (B, K, 3D) bf16.
+size_t split_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
+  if (!split_f32(D, dtype)) return 0;
+  return align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256) +
+         align_up(static_cast<size_t>(B * K * 3 * D) * 2, 256);
 }
 
 int check_dims(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
@@ -167,7 +183,7 @@ cudaStream_t as_stream(fkc_stream_t s) { return reinterpret_cast<cudaStream_t>(s
 size_t assign_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   if (!tc_shape_ok(D, dtype)) return 0;
   return align_up(static_cast<size_t>(B * N) * 32, 256) +
-         align_up(static_cast<size_t>(B * K) * 32, 256);
+         align_up(static_cast<size_t>(B * K) * 32, 256) + split_bytes(B, N, K, D, dtype);
 }
 
 struct LloydWs {
@@ -178,6 +194,8 @@ struct LloydWs {
   UpdatePlan plan{};          // fused update + finalize (single-GPU iteration)
   LoopCtl* ctl = nullptr;     // whole-loop graph control block
   uint8_t* splitk = nullptr;  // assign_splitk_bytes(), tensor-core path
+  uint8_t* x3 = nullptr;      // (B,N,3D) bf16, split-fp32 tensor-core path
+  uint8_t* c3 = nullptr;      // (B,K,3D) bf16, split-fp32 tensor-core path
 };
 
 constexpr size_t kCtlBytes = 256;
@@ -214,6 +232,12 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
     p += assign_splitk_bytes();
     out->aext = p;
     p += align_up(static_cast<size_t>(B * N) * 32, 256);
+    if (split_f32(D, dtype)) {
+      out->x3 = p;
+      p += align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256);
+      out->c3 = p;
+      p += align_up(static_cast<size_t>(B * K * 3 * D) * 2, 256);
+    }
   }
   out->upd = carve_update_workspace(p, B, N, K);
   p += update_workspace_bytes(B, N, K);
@@ -294,8 +318,12 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
   FKC_REQUIRE(x != nullptr && centroids != nullptr && ids != nullptr,
               "x, centroids and cluster_ids must be non-null");
   const cudaStream_t st = as_stream(stream);
-  if (use_tc(x, centroids, D, dtype)) {
-    const size_t need = assign_ws_bytes(B, N, K, D, dtype);
+  const bool split = split_f32(D, dtype);
+  const size_t need = assign_ws_bytes(B, N, K, D, dtype);
+  // fp32 callers without room for the split operands keep the CUDA-core kernel
+  // (fp32 needed no workspace before the split path existed).
+  if (use_tc(x, centroids, D, dtype) &&
+      !(split && (workspace == nullptr || workspace_bytes < need))) {
     if (workspace == nullptr || workspace_bytes < need)
       return set_error(FKC_EWORKSPACE, "assign workspace needs %zu bytes (got %zu)", need,
                        workspace_bytes);
@@ -305,6 +333,14 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
     uint8_t* cext = aext + align_up(static_cast<size_t>(B * N) * 32, 256);
     FKC_TRY(launch_xnorm_ext(x, aext, B, N, D, dtype, st));
     FKC_TRY(launch_cnorm_ext(centroids, c_sq, cext, nullptr, B, K, D, dtype, st));
+    if (split) {
+      uint8_t* x3 = cext + align_up(static_cast<size_t>(B * K) * 32, 256);
+      uint8_t* c3 = x3 + align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256);
+      FKC_TRY(launch_split_bf16(x, x3, B * N, D, true, st));
+      FKC_TRY(launch_split_bf16(centroids, c3, B * K, D, false, st));
+      return launch_assign_tc(x3, c3, aext, cext, ids, nullptr, nullptr, B, N, K, 3 * D,
+                              FKC_DTYPE_BF16, st);
+    }
     return launch_assign_tc(x, centroids, aext, cext, ids, nullptr, nullptr, B, N, K, D, dtype,
                             st);
   }
@@ -378,6 +414,7 @@ FKC_CAPI_EXPORT int fkc_lloyd_prepare(const void* x, int64_t B, int64_t N, int64
   // The fused update's per-cluster accumulators start (and stay) zero.
   FKC_TRY(launch_zero_fill(w.plan.done, w.plan.zero_bytes, as_stream(stream)));
   if (w.aext != nullptr) FKC_TRY(launch_xnorm_ext(x, w.aext, B, N, D, dtype, as_stream(stream)));
+  if (w.x3 != nullptr) FKC_TRY(launch_split_bf16(x, w.x3, B * N, D, true, as_stream(stream)));
   return FKC_OK;
 }
 
@@ -403,9 +440,16 @@ FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32
   FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
   const cudaStream_t st = as_stream(stream);
   FKC_TRY(launch_zero_fill(counts, static_cast<size_t>(B * K) * 4, st));
-  if (w.aext != nullptr && use_tc(x, centroids, D, dtype))
+  if (w.aext != nullptr && use_tc(x, centroids, D, dtype)) {
+    if (w.x3 != nullptr) {
+      // fp32: this iteration's centroids as split bf16 rows (x3: prepare).
+      FKC_TRY(launch_split_bf16(centroids, w.c3, B * K, D, false, st));
+      return launch_assign_tc(w.x3, w.c3, w.aext, w.cext, ids, counts, w.splitk, B, N, K, 3 * D,
+                              FKC_DTYPE_BF16, st);
+    }
     return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, w.splitk, B, N, K, D,
                             dtype, st);
+  }
   FKC_TRY(launch_assign_simt(x, centroids, nullptr, w.c_sq, ids, B, N, K, D, dtype, st));
   return launch_histogram(ids, counts, B, N, K, st);
 }

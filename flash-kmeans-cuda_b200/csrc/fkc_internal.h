@@ -83,6 +83,10 @@ int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D,
 // Centroid terms: extension rows cext[b,k,:] = {1,1,1,h1,h2,h3,0...} with
 // h = -0.5*c_sq (cext nullable) and/or c_sq_out[b,k] (nullable). c_sq is taken
 // from `c_sq` when non-null, otherwise computed from the centroids.
+// fp32 rows (rows x D) -> bf16 rows (rows x 3D) whose bf16 dot products give
+// fp32 dot products to ~2^-16: point side [hi|hi|lo], centroid side [hi|lo|hi].
+int launch_split_bf16(const void* src, void* dst, int64_t rows, int64_t D, bool point_side,
+                      cudaStream_t stream);
 int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
                      int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream);
 

@@ -77,7 +77,11 @@ def test_workspace_sizes_are_device_independent():
     # tensor-core shapes carry the norm-extension rows (32 B per point and per centroid)
     a = L.fkc_assign_workspace_size(1, 1000, 100, 128, 0)
     assert a >= 1000 * 32 + 100 * 32
-    assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == 0  # fp32: CUDA-core kernel
+    # fp32 with D <= 128: plus the split bf16 operand rows (3D bf16 per point and centroid)
+    al = lambda v: (v + 255) // 256 * 256
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == a + al(1000 * 384 * 2) + al(
+        100 * 384 * 2)
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 144, 2) == 0  # fp32, D > 128: CUDA cores
     assert L.fkc_assign_workspace_size(1, 1000, 100, 100, 0) == 0  # D % 16 != 0
     u = L.fkc_update_workspace_size(2, 1000, 100)
     assert u >= 2 * (2 * 1000 * 4 + 2 * 100 * 4)
@@ -105,6 +109,8 @@ def test_noalloc_rejects_oversize_before_any_cuda_call():
     assert L.fkc_assign_workspace_size(1, limit // 32 - 8192, 8192, 64, 0) == limit
     st = L.fkc_assign_noalloc(1, 1, None, None, 1, 1, limit // 32 - 8192 + 1, 8192, 64, 0, None)
     assert st == -5 and "static scratch" in _lib.last_error()
-    # shapes of the CUDA-core kernel need no scratch: the limit does not apply
+    # fp32 beyond the scratch falls back to the CUDA-core kernel: the limit does not apply
     st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 64, 2, None)
+    assert st == -1 and "non-null" in _lib.last_error()
+    st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 72, 2, None)
     assert st == -1 and "non-null" in _lib.last_error()
