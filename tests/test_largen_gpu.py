@@ -1,0 +1,60 @@
+"""Streamed large-N K-Means (host-resident x through one or two GPUs) against the
+device-resident Lloyd loop on the same data and initial centroids."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle.lloyd as orc
+from _data import mixture, subset_init, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, rel=2e-3):
+    a, b = to_np(a), to_np(b)
+    return np.abs(a - b) <= rel * np.abs(b) + 2 ** -9
+
+
+@pytest.mark.parametrize("dtype,devices", [("float16", 1), ("bfloat16", 1), ("float32", 1),
+                                           ("float16", 2)])
+def test_streamed_matches_resident(cuda_device, dtype, devices):
+    if torch.cuda.device_count() < devices:
+        pytest.skip(f"needs {devices} GPUs")
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+    from flash_kmeans_cuda.largen import kmeans_largeN
+
+    N, D, K = 50000, 128, 300
+    x = mixture(1, N, D, K, seed=81, dtype=dtype)
+    init = subset_init(x, K, seed=82)
+    # 7 blocks of 7168 rows (the last one shorter), dealt over the devices
+    ids_s, c_s, n_s = kmeans_largeN(x[0], K, max_iters=5, init_centroids=init[0],
+                                    devices=list(range(devices)), block_rows=7168)
+    ids_r, c_r, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=5, init_centroids=init.cuda())
+    torch.cuda.synchronize()
+    assert n_s == n_r == 5
+    assert ids_s.is_pinned() and ids_s.dtype == torch.int32 and ids_s.shape == (N,)
+    agree = (ids_s.numpy() == ids_r[0].cpu().numpy()).mean()
+    assert agree >= 0.999, agree
+    assert _close(c_s.cpu(), c_r[0].cpu()).mean() >= 0.999
+    # the final labels are the oracle's assignment against the centroids entering the
+    # last iteration: check them against a last streamed assignment step
+    from flash_kmeans_cuda.largen import kmeans_largeN_assign
+
+    ids_a = kmeans_largeN_assign(x[0], c_s, devices=list(range(devices)), block_rows=7168)
+    ref = orc.assign(to_np(x), to_np(c_s.cpu())[None])
+    assert not ((ids_a.numpy()[None] != ref.ids) & ref.gap_mask()).any()
+
+
+def test_streamed_tol_and_default_blocks(cuda_device):
+    from flash_kmeans_cuda.largen import kmeans_largeN
+
+    x = mixture(1, 30000, 64, 50, seed=91)[0]
+    init = x[torch.randperm(30000, generator=torch.Generator().manual_seed(5))[:50]]
+    ids, c, n = kmeans_largeN(x, 50, max_iters=60, tol=1e-3, init_centroids=init, devices=[0])
+    assert 1 <= n < 60
+    assert c.shape == (50, 64) and c.dtype == x.dtype and c.is_cuda
+    with pytest.raises(ValueError):
+        kmeans_largeN(x.cuda(), 50, max_iters=1, devices=[0])
