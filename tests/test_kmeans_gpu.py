@@ -121,6 +121,32 @@ def test_step_empty_and_split_clusters(cuda_device, dtype):
     assert not ((st.ids.cpu().numpy() != ref2.ids) & ref2.gap_mask()).any()
 
 
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+def test_local_update_small_clusters(cuda_device, dtype):
+    """fkc_lloyd_local (the multi-GPU rank's step before the sums reduction) on small,
+    skewed clusters with empty ones: sums and counts against the oracle, twice in a row."""
+    from flash_kmeans_cuda.kmeans import LloydState
+
+    B, N, K, D = 2, 12000, 600, 64
+    x = mixture(B, N, D, 40, seed=101, zipf=1.1, dtype=dtype)
+    c = subset_init(x, K, seed=102).float()
+    c[:, 500:] += 50.0  # 100 empty clusters per batch element
+    c = c.to(x.dtype)
+    st = LloydState(x.cuda(), K)
+    cd = c.cuda()
+    st.set_centroids(cd)
+    for _ in range(2):
+        st.local(cd)
+        torch.cuda.synchronize()
+        ids = st.ids.cpu().numpy()
+        s_ref, c_ref = orc.update(to_np(x), ids, K)
+        counts = st.counts.cpu().numpy()
+        assert np.array_equal(counts, c_ref)
+        assert counts.max() > 64 and (counts[:, 500:] == 0).all()
+        s_abs, _ = orc.update(np.abs(to_np(x)), ids, K)
+        assert (np.abs(st.sums.cpu().numpy() - s_ref) <= 1e-5 * s_abs + 1e-6).all()
+
+
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
 def test_free_running_inertia(cuda_device, dtype):
     from flash_kmeans_cuda import batch_kmeans_Euclid

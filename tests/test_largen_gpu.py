@@ -38,7 +38,18 @@ def test_streamed_matches_resident(cuda_device, dtype, devices):
     assert ids_s.is_pinned() and ids_s.dtype == torch.int32 and ids_s.shape == (N,)
     agree = (ids_s.numpy() == ids_r[0].cpu().numpy()).mean()
     assert agree >= 0.999, agree
-    assert _close(c_s.cpu(), c_r[0].cpu()).mean() >= 0.999
+    # free-running comparison (a near-tie flip moves its clusters' means): >= 99% of the
+    # centroid entries close and the final inertia within 0.05%
+    assert _close(c_s.cpu(), c_r[0].cpu()).mean() >= 0.99
+    xn = to_np(x)[0].astype(np.float64)
+
+    def inertia(ids, c):
+        cn = to_np(c).astype(np.float64)
+        return float(((xn - cn[ids]) ** 2).sum())
+
+    i_s = inertia(ids_s.numpy(), c_s.cpu())
+    i_r = inertia(ids_r[0].cpu().numpy(), c_r[0].cpu())
+    assert abs(i_s - i_r) <= 5e-4 * i_r, (i_s, i_r)
     # the final labels are the oracle's assignment against the centroids entering the
     # last iteration: check them against a last streamed assignment step
     from flash_kmeans_cuda.largen import kmeans_largeN_assign
