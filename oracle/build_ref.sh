@@ -1,6 +1,7 @@
 #!/bin/bash
 # Builds the reference comparator from the reference's own sources, in place
-# under /root/reference (read-only; nothing is copied), into oracle/_ref/:
+# in the reference checkout given by FKC_REFERENCE_ROOT (read-only; nothing is
+# copied), into oracle/_ref/:
 #   libfkc_ref.so      - flash_kmeans_cuda/csrc/{api.cpp, assign/*.cu, update/*.cu}
 #                        compiled with the reference's flags (setup.py:78-85) for
 #                        compute_100/sm_100 (setup.py:55), linked against libtorch;
