@@ -36,6 +36,7 @@ _SIGNATURES = {
     "fkc_status_string": (ctypes.c_char_p, [c_int]),
     "fkc_device_supported": (c_int, []),
     "fkc_device_status": (c_int, []),
+    "fkc_selftest_wait_timeout": (c_int, [ctypes.c_uint32, c_vp]),
     "fkc_assign_workspace_size": (c_size, [c_i64, c_i64, c_i64, c_i64, c_int]),
     "fkc_assign": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_int,
                            c_vp, c_size, c_vp]),

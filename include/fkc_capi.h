@@ -73,6 +73,14 @@ FKC_CAPI_EXPORT uint64_t fkc_kernel_launches(void);
  * call (the record is cleared). Use in tests and health checks. */
 FKC_CAPI_EXPORT int fkc_device_status(void);
 
+/* Test of the device-side failure path, without a fault: launches a one-warp
+ * kernel whose bounded mbarrier wait (the wait the assignment pipeline uses)
+ * can never complete. After timeout_us (1 .. 10^7) it gives up, records site
+ * code 199 in the device error word and returns, so the next
+ * fkc_device_status() returns FKC_ETIMEOUT and the context stays usable.
+ * No counterpart in the reference. */
+FKC_CAPI_EXPORT int fkc_selftest_wait_timeout(uint32_t timeout_us, fkc_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Assignment
  *   ids[b,n] = argmin_k ||x[b,n,:] - c[b,k,:]||^2, ties -> lowest k.
