@@ -516,10 +516,14 @@ def run_ours(args, w: dict) -> None:
                        "frac": update_bytes / (t_update * 1e-3) / 1e9 / peaks["hbm"],
                        "algorithmic_bytes": update_bytes,
                        "note": "phase times of the stepwise entry points (fkc_lloyd_update, "
-                               "fkc_lloyd_finalize); the timed step (fkc_lloyd_iter) "
-                               + ("fuses update and finalize into one pass over the clusters"
+                               "fkc_lloyd_finalize); "
+                               + ("the timed step (fkc_lloyd_iter) fuses update and finalize "
+                                  "into one pass over the clusters"
                                   if world == 1 and Nl <= 32 * K else
-                                  "runs the same update and finalize")},
+                                  "the timed step (fkc_lloyd_iter) runs the same update and "
+                                  "finalize" if world == 1 else
+                                  "the timed step runs this rank's update, then reduces sums and "
+                                  "counts across ranks inside the finalize")},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
