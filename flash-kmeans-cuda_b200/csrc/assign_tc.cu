@@ -57,6 +57,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -988,13 +989,14 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
     cfg.numAttrs = 1;
     // Number of CTA pairs the device can hold at once (a persistent grid must
     // not exceed it: pairs beyond it would wait for a second wave).
-    static int pairs_cached[64] = {};
-    int& pairs = pairs_cached[di->device & 63];
+    static std::atomic<int> pairs_cached[64] = {};  // per device; racing threads store the same
+    int pairs = pairs_cached[di->device & 63].load(std::memory_order_relaxed);
     if (pairs == 0) {
       cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
       int clusters = 0;
       FKC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
       pairs = clusters > 0 ? clusters : -1;
+      pairs_cached[di->device & 63].store(pairs, std::memory_order_relaxed);
     }
     FKC_REQUIRE(pairs > 0, "assign: this device cannot co-schedule 2-CTA clusters");
     units = pairs;

@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "fkc_common.cuh"
@@ -766,8 +767,14 @@ int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, fl
   constexpr int R = 2 * L;
   constexpr int P = R < 8 ? R : 8;
   auto kern = gather_accumulate_kernel<T, L, P>;
-  static int cap = 0;  // resident blocks; the same on every device of one model
-  if (cap == 0) cap = resident_blocks(kern);
+  // Resident blocks (the same on every device of one model). Host threads
+  // driving several GPUs may race on the first call: atomic, same value.
+  static std::atomic<int> cap_cache{0};
+  int cap = cap_cache.load(std::memory_order_relaxed);
+  if (cap == 0) {
+    cap = resident_blocks(kern);
+    cap_cache.store(cap, std::memory_order_relaxed);
+  }
   // About one span per resident warp, spans a multiple of 64 positions.
   const int64_t warps = static_cast<int64_t>(cap) * 8;
   int64_t spans_per_batch = std::max<int64_t>(1, (warps + B - 1) / B);
@@ -935,8 +942,14 @@ int launch_gather_finalize(const T* x, const UpdateWorkspace& w, const UpdatePla
                            int64_t K, cudaStream_t stream) {
   constexpr int P = L >= 16 ? 16 : 8;  // row loads in flight per group
   auto kern = gather_finalize_kernel<T, L, P>;
-  static int cap = 0;  // resident blocks; the same on every device of one model
-  if (cap == 0) cap = resident_blocks(kern);
+  // Resident blocks (the same on every device of one model). Host threads
+  // driving several GPUs may race on the first call: atomic, same value.
+  static std::atomic<int> cap_cache{0};
+  int cap = cap_cache.load(std::memory_order_relaxed);
+  if (cap == 0) {
+    cap = resident_blocks(kern);
+    cap_cache.store(cap, std::memory_order_relaxed);
+  }
   constexpr int G = 32 / L;
   const int64_t units = B * K + B * static_cast<int64_t>(plan.cap);
   const int64_t blocks = std::min<int64_t>((units + 8 * G - 1) / (8 * G), cap);
