@@ -114,3 +114,11 @@ def test_noalloc_rejects_oversize_before_any_cuda_call():
     assert st == -1 and "non-null" in _lib.last_error()
     st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 72, 2, None)
     assert st == -1 and "non-null" in _lib.last_error()
+
+
+def test_selftest_timeout_checked_before_any_cuda_call():
+    from flash_kmeans_cuda import _lib
+
+    assert _lib.lib.fkc_selftest_wait_timeout(0, None) == -1
+    assert "timeout_us" in _lib.last_error()
+    assert _lib.lib.fkc_selftest_wait_timeout(20_000_000, None) == -1
