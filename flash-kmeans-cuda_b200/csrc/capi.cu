@@ -254,8 +254,15 @@ int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* cou
     FKC_TRY(launch_zero_fill(counts, static_cast<size_t>(B * K) * 4, st));
     FKC_TRY(launch_histogram(ids, counts, B, N, K, st));
   }
-  FKC_TRY(launch_counting_sort(ids, counts, uw, B, N, K, counts_ready, st));
-  FKC_TRY(launch_zero_fill(sums, static_cast<size_t>(B * K * D) * 4, st));
+  UpdateWorkspace w = uw;
+  if (aligned16(sums)) {
+    // the scatter kernel zeroes sums (no separate fill launch)
+    w.zero_f32 = sums;
+    w.zero_count = B * K * D;
+  }
+  FKC_TRY(launch_counting_sort(ids, counts, w, B, N, K, counts_ready, st));
+  if (w.zero_f32 == nullptr)
+    FKC_TRY(launch_zero_fill(sums, static_cast<size_t>(B * K * D) * 4, st));
   return launch_run_accumulate(x, uw.perm, uw.ids_sorted, sums, nullptr, B, N, K, D, dtype, st);
 }
 

@@ -107,6 +107,10 @@ struct UpdateWorkspace {
   int32_t* cursor;      // (B, K) scatter cursors
   int32_t* perm;        // (B, N) row index in cluster order
   int32_t* ids_sorted;  // (B, N) label in cluster order
+  // Optional: zero_count floats at zero_f32 (16-byte aligned) are zeroed by the
+  // scatter kernel after its dependency wait (saves a separate fill launch).
+  float* zero_f32 = nullptr;
+  int64_t zero_count = 0;
 };
 size_t update_workspace_bytes(int64_t B, int64_t N, int64_t K);
 UpdateWorkspace carve_update_workspace(void* ws, int64_t B, int64_t N, int64_t K);

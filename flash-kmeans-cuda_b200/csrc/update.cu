@@ -177,6 +177,17 @@ __global__ void __launch_bounds__(kScanThreads) scan_kernel(
   if (PLAN && t == 0) extra_count[blockIdx.x] = xcarry;
 }
 
+// Grid-stride zero fill of n floats at p (16-byte aligned), folded into the
+// scatter kernels after their dependency wait.
+__device__ __forceinline__ void zero_floats(float* p, int64_t n) {
+  if (p == nullptr) return;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  float4* p4 = reinterpret_cast<float4*>(p);
+  for (int64_t i = t0; i < n / 4; i += stride) p4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i = (n / 4) * 4 + t0; i < n; i += stride) p[i] = 0.f;
+}
+
 // Chunked scatter (K <= kLocalMaxK): the CTA ranks its rows per cluster with
 // shared-memory atomics, claims slots [base, base + local count) of each
 // cluster it holds with one global atomic on cursor, then writes
@@ -188,8 +199,10 @@ constexpr int kLocalMaxK = 16384;  // 64 KB of shared-memory counters
 template <int RPT>
 __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
     const int32_t* __restrict__ ids, int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
-    int32_t* __restrict__ ids_sorted, int N, int K, int chunks_per_batch) {
+    int32_t* __restrict__ ids_sorted, int N, int K, int chunks_per_batch, float* zero_p,
+    int64_t zero_n) {
   pdl_wait();
+  zero_floats(zero_p, zero_n);
   extern __shared__ int cnt[];  // K counters, then reused for the K slot bases
   const int t = threadIdx.x;
   const int b = blockIdx.x / chunks_per_batch;
@@ -236,8 +249,9 @@ __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
 __global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
                                       int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
                                       int32_t* __restrict__ ids_sorted, int64_t total, int64_t N,
-                                      int K) {
+                                      int K, float* zero_p, int64_t zero_n) {
   pdl_wait();
+  zero_floats(zero_p, zero_n);
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
@@ -864,7 +878,8 @@ int launch_scatter_chunk(const int32_t* ids, const UpdateWorkspace& w, int64_t B
   FKC_REQUIRE(chunks * B < (1ll << 31), "update: too many row chunks");
   return launch_pdl(kern, dim3(static_cast<unsigned>(chunks * B)), dim3(kSortThreads),
                     static_cast<size_t>(smem), stream, ids, w.cursor, w.perm, w.ids_sorted,
-                    static_cast<int>(N), static_cast<int>(K), static_cast<int>(chunks));
+                    static_cast<int>(N), static_cast<int>(K), static_cast<int>(chunks),
+                    w.zero_f32, w.zero_count);
 }
 
 }  // namespace
@@ -886,7 +901,8 @@ int launch_scatter(const int32_t* ids, const UpdateWorkspace& w, int64_t B, int6
   }
   const int64_t total = B * N;
   return launch_pdl(scatter_atomic_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream, ids,
-                    w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K));
+                    w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K), w.zero_f32,
+                    w.zero_count);
 }
 
 }  // namespace
