@@ -17,6 +17,13 @@
 //     lanes x 16 B). Each stream keeps P rows in flight (16-byte non-allocating
 //     loads), accumulates in registers and flushes every run with 16-byte
 //     vector atomics (red.global.add.v4.f32). No sorted copy of x is written.
+//   * the scatter kernel also zeroes the sums the accumulator adds into;
+//   * with at most 32 rows per cluster on average, a single-GPU Lloyd step
+//     replaces accumulate + finalize by one pass over the clusters
+//     (gather_finalize_kernel): whole clusters are summed in row order and
+//     finished with plain stores; clusters of more than 64 rows are cut into
+//     pieces (laid out by the scan) that add into a per-cluster row, and the
+//     last piece finishes the cluster.
 // The same accumulator serves the reference's _C.centroid_update_sorted and
 // _C.centroid_update_sorted_indexed entry points (perm == nullptr for the
 // former).
