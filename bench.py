@@ -301,7 +301,9 @@ def run_reference_arm(args, w: dict) -> None:
         return
     from oracle.cpu_lloyd import lloyd_cpu
 
-    n_s, _ = cpu_sample_rows(w, target_s=1.0)
+    # About a second per step, less for long runs: the whole arm stays near two minutes.
+    target = min(1.0, 120.0 / max(1, args.steps + args.warmup))
+    n_s, _ = cpu_sample_rows(w, target_s=target)
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     x = torch.randn((1, n_s, w["D"]), generator=g)
