@@ -417,8 +417,9 @@ def run_ours(args, w: dict) -> None:
     other = bufs[(args.warmup + args.steps + 1) % 2]
     reps = 5
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-    t_assign = t_update = t_fin = 0.0
+    t_assign = t_update = t_fin = t_iter = 0.0
     dims = (Bl, Nl, K, D, st.code, st.ws.data_ptr(), st.ws_bytes)
+    ev.append(torch.cuda.Event(enable_timing=True))
     for _ in range(reps + 1):
         barrier_sync(dev)
         sp = stream.cuda_stream
@@ -434,12 +435,20 @@ def run_ours(args, w: dict) -> None:
                                                cur_c.data_ptr(), other.data_ptr(), None, *dims,
                                                sp), "finalize")
         ev[3].record(stream)
+        if world == 1:
+            # the whole step as timed above (fkc_lloyd_iter; its update + finalize is one
+            # fused pass when clusters are small)
+            _lib.check(_lib.lib.fkc_lloyd_iter(x.data_ptr(), cur_c.data_ptr(), other.data_ptr(),
+                                               st.ids.data_ptr(), st.sums.data_ptr(),
+                                               st.counts.data_ptr(), None, *dims, sp), "iter")
+        ev[4].record(stream)
         torch.cuda.synchronize(dev)
         if _ == 0:
             continue  # warm-up rep
         t_assign += ev[0].elapsed_time(ev[1]) / reps
         t_update += ev[1].elapsed_time(ev[2]) / reps
         t_fin += ev[2].elapsed_time(ev[3]) / reps
+        t_iter += ev[3].elapsed_time(ev[4]) / reps
     t_assign = max_over_ranks(t_assign, dev)
     t_update = max_over_ranks(t_update, dev)
     t_fin = max_over_ranks(t_fin, dev)
@@ -509,6 +518,10 @@ def run_ours(args, w: dict) -> None:
                               if B * N * D * esz > L2_BYTES else "x fits in L2")},
             "assign_tflops": tflops,
             "assign_ms": t_assign, "update_ms": t_update, "finalize_ms": t_fin,
+            # one whole step (assign + update + finalize) timed alone, and what the step
+            # spends after its assign (the fused pass when clusters are small)
+            "step_ms": (t_iter if world == 1 else None),
+            "step_after_assign_ms": (max(t_iter - t_assign, 0.0) if world == 1 else None),
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak,
                          "unit": "TFLOP/s", "frac": tflops / peak,
                          "traffic": traffic, "kernel": "assign_tc_kernel",
