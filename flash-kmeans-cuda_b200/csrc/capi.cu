@@ -247,14 +247,17 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
 
 // counts_ready: counts already holds the histogram of `ids` (fkc_lloyd_assign),
 // whose labels all lie in [0,K).
+// zero_scalar (nullable): one float the scatter also zeroes (the step's shift).
 int update_from_ids(const void* x, const int32_t* ids, float* sums, int32_t* counts,
                     bool counts_ready, const UpdateWorkspace& uw, int64_t B, int64_t N,
-                    int64_t K, int64_t D, int dtype, cudaStream_t st) {
+                    int64_t K, int64_t D, int dtype, cudaStream_t st,
+                    float* zero_scalar = nullptr) {
   if (!counts_ready) {
     FKC_TRY(launch_zero_fill(counts, static_cast<size_t>(B * K) * 4, st));
     FKC_TRY(launch_histogram(ids, counts, B, N, K, st));
   }
   UpdateWorkspace w = uw;
+  w.zero_scalar = zero_scalar;
   if (aligned16(sums)) {
     // the scatter kernel zeroes sums (no separate fill launch)
     w.zero_f32 = sums;
@@ -517,10 +520,17 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
     return launch_update_finalize(x, ids, counts, w.upd, w.plan, old_c, new_c, sums, w.c_sq,
                                   w.cext, shift_out, B, N, K, D, dtype, as_stream(stream));
   }
-  FKC_TRY(fkc_lloyd_local(x, old_c, ids, sums, counts, B, N, K, D, dtype, workspace,
-                          workspace_bytes, stream));
-  return fkc_lloyd_finalize(sums, counts, old_c, new_c, shift_out, B, N, K, D, dtype, workspace,
-                            workspace_bytes, stream);
+  // assign -> counting sort + accumulate (the scatter also zeroes the shift)
+  // -> finalize
+  FKC_TRY(fkc_lloyd_assign(x, old_c, ids, counts, B, N, K, D, dtype, workspace, workspace_bytes,
+                           stream));
+  FKC_REQUIRE(old_c && new_c && sums, "null argument");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  const cudaStream_t st = as_stream(stream);
+  FKC_TRY(update_from_ids(x, ids, sums, counts, true, w.upd, B, N, K, D, dtype, st, shift_out));
+  return launch_finalize(sums, counts, old_c, new_c, w.c_sq, w.cext, shift_out, B, K, D, dtype,
+                         st, /*shift_zeroed=*/shift_out != nullptr);
 }
 
 FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem(

@@ -302,9 +302,10 @@ int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, con
 
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,
-                    int64_t D, int dtype, cudaStream_t stream) {
+                    int64_t D, int dtype, cudaStream_t stream, bool shift_zeroed) {
   const int64_t rows = B * K;
-  if (shift_out != nullptr) FKC_TRY(launch_zero_fill(shift_out, sizeof(float), stream));
+  if (shift_out != nullptr && !shift_zeroed)
+    FKC_TRY(launch_zero_fill(shift_out, sizeof(float), stream));
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   int64_t grid = (rows + 7) / 8;

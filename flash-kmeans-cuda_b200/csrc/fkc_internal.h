@@ -111,6 +111,7 @@ struct UpdateWorkspace {
   // scatter kernel after its dependency wait (saves a separate fill launch).
   float* zero_f32 = nullptr;
   int64_t zero_count = 0;
+  float* zero_scalar = nullptr;  // one float zeroed likewise (the shift of the step)
 };
 size_t update_workspace_bytes(int64_t B, int64_t N, int64_t K);
 UpdateWorkspace carve_update_workspace(void* ws, int64_t B, int64_t N, int64_t K);
@@ -193,8 +194,9 @@ int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, con
                              unsigned int* mc_shift, float* shift_clear, int64_t row0,
                              int64_t row1, int64_t D, int dtype, cudaStream_t stream);
 
+// shift_zeroed: *shift_out is already 0 (the scatter of this step zeroed it).
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,
                     float* c_sq_out, void* cext_out, float* shift_out, int64_t B, int64_t K,
-                    int64_t D, int dtype, cudaStream_t stream);
+                    int64_t D, int dtype, cudaStream_t stream, bool shift_zeroed = false);
 
 }  // namespace fkc

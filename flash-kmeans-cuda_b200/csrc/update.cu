@@ -207,9 +207,10 @@ template <int RPT>
 __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
     const int32_t* __restrict__ ids, int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
     int32_t* __restrict__ ids_sorted, int N, int K, int chunks_per_batch, float* zero_p,
-    int64_t zero_n) {
+    int64_t zero_n, float* zero_one) {
   pdl_wait();
   zero_floats(zero_p, zero_n);
+  if (zero_one != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero_one = 0.f;
   extern __shared__ int cnt[];  // K counters, then reused for the K slot bases
   const int t = threadIdx.x;
   const int b = blockIdx.x / chunks_per_batch;
@@ -256,9 +257,10 @@ __global__ void __launch_bounds__(kSortThreads) scatter_chunk_kernel(
 __global__ void scatter_atomic_kernel(const int32_t* __restrict__ ids,
                                       int32_t* __restrict__ cursor, int32_t* __restrict__ perm,
                                       int32_t* __restrict__ ids_sorted, int64_t total, int64_t N,
-                                      int K, float* zero_p, int64_t zero_n) {
+                                      int K, float* zero_p, int64_t zero_n, float* zero_one) {
   pdl_wait();
   zero_floats(zero_p, zero_n);
+  if (zero_one != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero_one = 0.f;
   const int lane = threadIdx.x & 31;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
@@ -886,7 +888,7 @@ int launch_scatter_chunk(const int32_t* ids, const UpdateWorkspace& w, int64_t B
   return launch_pdl(kern, dim3(static_cast<unsigned>(chunks * B)), dim3(kSortThreads),
                     static_cast<size_t>(smem), stream, ids, w.cursor, w.perm, w.ids_sorted,
                     static_cast<int>(N), static_cast<int>(K), static_cast<int>(chunks),
-                    w.zero_f32, w.zero_count);
+                    w.zero_f32, w.zero_count, w.zero_scalar);
 }
 
 }  // namespace
@@ -909,7 +911,7 @@ int launch_scatter(const int32_t* ids, const UpdateWorkspace& w, int64_t B, int6
   const int64_t total = B * N;
   return launch_pdl(scatter_atomic_kernel, dim3(grid_for(total, 256)), dim3(256), 0, stream, ids,
                     w.cursor, w.perm, w.ids_sorted, total, N, static_cast<int>(K), w.zero_f32,
-                    w.zero_count);
+                    w.zero_count, w.zero_scalar);
 }
 
 }  // namespace
