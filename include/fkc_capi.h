@@ -89,7 +89,11 @@ FKC_CAPI_EXPORT int fkc_selftest_wait_timeout(uint32_t timeout_us, fkc_stream_t 
  *   read only by the fp32 / odd-D fallback, which clamps distances at 0 as
  *   the reference's safe kernel does; the tensor-core path ignores it (as the
  *   reference's raw-distance mma path does).
- *   fp16/bf16 with D % 16 == 0 and D <= 384 run the tcgen05 kernel.
+ *   fp16/bf16 with D % 16 == 0 and D <= 384 run the tcgen05 kernel; so does
+ *   fp32 with D % 16 == 0 and D <= 128 (x and c as split bf16 rows of 3D:
+ *   hi.hi + hi.lo + lo.hi, ~2^-16 relative), when the workspace holds those
+ *   rows (fkc_assign_workspace_size counts them); fp32 with a smaller or no
+ *   workspace keeps the CUDA-core kernel.
  * Replaces: _C.euclid_assign (csrc/bindings.cpp:43-71),
  *           fkc::euclid_assign_out (csrc/api.cpp:58-72),
  *           launch_assign_sm80 / launch_assign_safe (csrc/assign/assign.h:32-44).
