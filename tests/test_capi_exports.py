@@ -122,3 +122,45 @@ def test_selftest_timeout_checked_before_any_cuda_call():
     assert _lib.lib.fkc_selftest_wait_timeout(0, None) == -1
     assert "timeout_us" in _lib.last_error()
     assert _lib.lib.fkc_selftest_wait_timeout(20_000_000, None) == -1
+
+
+def test_lloyd_entry_points_check_arguments_on_the_host():
+    """Argument errors of the Lloyd entry points come back before any CUDA call."""
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    # fkc_lloyd_run: negative max_iters
+    st = L.fkc_lloyd_run(1, 1, 1, 1, 1, 1, None, -1, 0.0, 1, 100, 8, 16, 0, 1, 1 << 20, None)
+    assert st == -1 and "max_iters" in _lib.last_error()
+    # fkc_lloyd_run: null centroids
+    st = L.fkc_lloyd_run(1, None, 1, 1, 1, 1, None, 5, 0.0, 1, 100, 8, 16, 0, 1, 1 << 20, None)
+    assert st == -1
+    # fkc_lloyd_iter without a workspace of the documented size
+    need = L.fkc_lloyd_workspace_size(1, 100, 8, 16, 0)
+    st = L.fkc_lloyd_iter(1, 1, 1, 1, 1, 1, None, 1, 100, 8, 16, 0, 256, need - 1, None)
+    assert st == -5 and "workspace" in _lib.last_error()
+    # fkc_lloyd_finalize_multimem: row slice outside [0, B*K)
+    st = L.fkc_lloyd_finalize_multimem(1, 1, 1, 1, 1, None, None, 0, 17, 2, 8, 16, 0, None)
+    assert st == -1 and "rows" in _lib.last_error()
+    # fkc_update: workspace too small
+    st = L.fkc_update(1, 1, 1, 1, 1, 100, 8, 16, 0, 256, 1, None)
+    assert st == -5 and "workspace" in _lib.last_error()
+    # bad dtype code
+    st = L.fkc_lloyd_assign(1, 1, 1, 1, 1, 100, 8, 16, 7, 256, 1 << 20, None)
+    assert st == -1 and "dtype" in _lib.last_error()
+
+
+def test_fp32_workspace_grows_with_the_split_rows():
+    """fp32 rows of D <= 128 add 3*D bf16 per point and per centroid to the Lloyd
+    workspace (the split operands of the tensor-core path); D > 128 does not."""
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    al = lambda v: (v + 255) // 256 * 256
+    f16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 128, 0)
+    f32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 128, 2)
+    # the rest of the layout is the same for both types
+    assert f32 - f16 == al(5000 * 384 * 2) + al(300 * 384 * 2)
+    w144_16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 144, 0)
+    w144_32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 144, 2)
+    assert w144_32 < w144_16  # fp32 D=144: no tensor-core rows at all
