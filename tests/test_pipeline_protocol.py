@@ -1,0 +1,189 @@
+"""The assignment kernel's mbarrier protocol, simulated on the CPU (no GPU).
+
+Each role of a CTA (TMA producer warp, MMA lane, each epilogue warp) runs as a
+coroutine that performs the same barrier operations, in the same order and with the same
+phase parities, as assign_tc.cu: waits on c_full/c_empty (centroid stages), x_full/x_empty
+(row-tile buffers), acc_full/acc_empty (TMEM slots), merge_full/merge_empty (per-row best
+exchange between the two column slices, crossed and deferred to the next tile). Copies
+and MMAs complete at once. A scheduler runs whatever can run; the test fails if a state
+is reached where no role can make progress before all have finished (a deadlock in the
+kernel would be a wait that expires). Checked for every configuration the dispatch uses
+(stages, slots, one or two row-tile buffers, sub-tile owners or column slices) and for
+whole-tile and split-mode work lists."""
+
+from __future__ import annotations
+
+import itertools
+
+import pytest
+
+from test_split_mode_plan import segments
+
+
+class Bar:
+    def __init__(self, count):
+        self.count, self.pending, self.phase = count, count, 0
+
+    def arrive(self):
+        self.pending -= 1
+        assert self.pending >= 0
+        if self.pending == 0:
+            self.pending = self.count
+            self.phase += 1
+
+    def done(self, parity):
+        # try_wait.parity(P): the phase of parity P has completed
+        return (self.phase & 1) != parity
+
+
+def wait(bar, parity):
+    while not bar.done(parity):
+        yield
+
+
+def producer(B, segs, MT, ST, XS, nchunks):
+    c_it = x_it = 0
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            st, ph = c_it % ST, (c_it // ST) & 1
+            yield from wait(B["c_empty"][st], ph ^ 1)
+            B["c_full"][st].arrive()
+            c_it += 1
+            if ch == ch0:
+                xb, xph = x_it % XS, (x_it // XS) & 1
+                for s in range(MT):
+                    xi = xb * MT + s
+                    yield from wait(B["x_empty"][xi], xph ^ 1)
+                    B["x_full"][xi].arrive()
+        x_it += 1
+
+
+def mma(B, segs, MT, ST, XS, slots):
+    c_it = x_it = item = 0
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            st, ph = c_it % ST, (c_it // ST) & 1
+            yield from wait(B["c_full"][st], ph)
+            for s in range(MT):
+                xi = (x_it % XS) * MT + s
+                if ch == ch0:
+                    yield from wait(B["x_full"][xi], (x_it // XS) & 1)
+                slot = item % slots
+                yield from wait(B["acc_empty"][slot], ((item // slots) & 1) ^ 1)
+                B["acc_full"][slot].arrive()  # tcgen05.commit
+                if ch == ch1 - 1:
+                    B["x_empty"][xi].arrive()
+                item += 1
+            B["c_empty"][st].arrive()
+            c_it += 1
+        x_it += 1
+
+
+def owner_warp(B, segs, MT, slots, part):
+    item = 0
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            for s in range(MT):
+                if s == part:
+                    slot = item % slots
+                    yield from wait(B["acc_full"][slot], (item // slots) & 1)
+                    B["acc_empty"][slot].arrive()
+                item += 1
+
+
+def slice_warp(B, segs, MT, slots, part):
+    peer = part ^ 1
+    owns = part < MT
+    sends = MT > 1 or part == 1
+    item = tcount = 0
+    pending = False
+
+    def finish():
+        nonlocal pending
+        yield from wait(B["merge_full"][peer], (tcount & 1) ^ 1)
+        B["merge_empty"][peer].arrive()
+        pending = False
+
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            for s in range(MT):
+                slot = item % slots
+                yield from wait(B["acc_full"][slot], (item // slots) & 1)
+                B["acc_empty"][slot].arrive()
+                item += 1
+                if pending:
+                    yield from finish()
+        if sends:
+            yield from wait(B["merge_empty"][part], (tcount & 1) ^ 1)
+            B["merge_full"][part].arrive()
+        if owns:
+            pending = True
+        tcount += 1
+    if pending:
+        yield from finish()
+
+
+def run_cta(segs, MT, ST, NC, XS, own, nchunks, acc_empty_count=None):
+    slots = 512 // NC
+    if acc_empty_count is None:
+        acc_empty_count = 4 if own else 8
+    B = {
+        "c_full": [Bar(1) for _ in range(ST)], "c_empty": [Bar(1) for _ in range(ST)],
+        "x_full": [Bar(1) for _ in range(XS * MT)], "x_empty": [Bar(1) for _ in range(XS * MT)],
+        "acc_full": [Bar(1) for _ in range(slots)],
+        "acc_empty": [Bar(acc_empty_count) for _ in range(slots)],
+        "merge_full": [Bar(4) for _ in range(2)], "merge_empty": [Bar(4) for _ in range(2)],
+    }
+    roles = [producer(B, segs, MT, ST, XS, nchunks), mma(B, segs, MT, ST, XS, slots)]
+    for w in range(8):  # epilogue warps 2..9: half = (w >> 2)
+        part = w >> 2
+        roles.append(owner_warp(B, segs, MT, slots, part) if own
+                     else slice_warp(B, segs, MT, slots, part))
+    live = list(roles)
+
+    def state():
+        return [(b.phase, b.pending) for v in B.values() for b in v]
+
+    while live:
+        # one sweep: every live role runs until it blocks (yields) or finishes
+        before, finished = state(), False
+        for r in list(live):
+            try:
+                next(r)
+            except StopIteration:
+                live.remove(r)
+                finished = True
+        if not finished and state() == before:
+            raise AssertionError("deadlock: no role can make progress")
+
+
+# (DB, MT, NC, ST) of the single-CTA dispatch, with kXS and ownership as the kernel derives
+CONFIGS = [
+    # D <= 64: two x buffers, sub-tile owners
+    dict(MT=2, NC=256, ST=3, XS=2, own=True),
+    # D <= 128: column slices with the crossed, deferred merge
+    dict(MT=2, NC=256, ST=2, XS=1, own=False),
+    # D <= 192: 128-centroid chunks, owners, four slots
+    dict(MT=2, NC=128, ST=2, XS=1, own=True),
+    # D <= 256 (MT = 1): column slices, slice 1 sends, slice 0 finishes
+    dict(MT=1, NC=128, ST=2, XS=1, own=False),
+]
+
+
+@pytest.mark.parametrize("cfg", CONFIGS, ids=lambda c: "-".join(f"{k}{v}" for k, v in c.items()))
+@pytest.mark.parametrize("total_tiles,nchunks,units", [(7, 1, 3), (9, 4, 4), (20, 3, 6),
+                                                       (5, 8, 3), (13, 2, 13), (300, 2, 148)])
+def test_no_deadlock(cfg, total_tiles, nchunks, units):
+    # whole-tile mode (tile, tile + units, ...) and split mode (contiguous unit ranges)
+    for unit in range(min(units, 6)):
+        whole = [(t, 0, nchunks) for t in range(unit, total_tiles, units)]
+        run_cta(whole, nchunks=nchunks, **cfg)
+        if total_tiles * nchunks >= units:
+            run_cta(segments(unit, units, total_tiles, nchunks), nchunks=nchunks, **cfg)
+
+
+def test_simulator_detects_a_broken_protocol():
+    # one arrival too many expected on the slot barriers: the MMA must stall for good
+    with pytest.raises(AssertionError, match="deadlock"):
+        run_cta([(0, 0, 4), (1, 0, 4)], MT=2, ST=2, NC=256, XS=1, own=False, nchunks=4,
+                acc_empty_count=9)
