@@ -187,3 +187,85 @@ def test_simulator_detects_a_broken_protocol():
     with pytest.raises(AssertionError, match="deadlock"):
         run_cta([(0, 0, 4), (1, 0, 4)], MT=2, ST=2, NC=256, XS=1, own=False, nchunks=4,
                 acc_empty_count=9)
+
+
+def run_pair(segs, MT, ST, NC, XS, own, nchunks):
+    """CTA pair (cta_group::2): both CTAs load their halves into the leader's full
+    barriers (modelled as one arrival each), the leader's MMA lane commits to both CTAs'
+    empty/full barriers (multicast), and both CTAs' epilogue warps release the leader's
+    slot barriers."""
+    slots = 512 // NC
+    per = 4 if own else 8
+
+    def cta_bars():
+        return {
+            "c_full": [Bar(2) for _ in range(ST)], "c_empty": [Bar(1) for _ in range(ST)],
+            "x_full": [Bar(2) for _ in range(XS * MT)],
+            "x_empty": [Bar(1) for _ in range(XS * MT)],
+            "acc_full": [Bar(1) for _ in range(slots)],
+            "acc_empty": [Bar(2 * per) for _ in range(slots)],
+            "merge_full": [Bar(4) for _ in range(2)], "merge_empty": [Bar(4) for _ in range(2)],
+        }
+
+    lead, follow = cta_bars(), cta_bars()
+
+    class Multicast:
+        """Commit targets: the same barrier in both CTAs."""
+
+        def __init__(self, a, b):
+            self.a, self.b = a, b
+
+        def arrive(self):
+            self.a.arrive()
+            self.b.arrive()
+
+    mma_view = dict(lead)
+    for k in ("c_empty", "x_empty", "acc_full"):
+        mma_view[k] = [Multicast(a, b) for a, b in zip(lead[k], follow[k])]
+
+    def producer_of(own_bars):
+        view = dict(own_bars)
+        view["c_full"], view["x_full"] = lead["c_full"], lead["x_full"]
+        return producer(view, segs, MT, ST, XS, nchunks)
+
+    def epi_of(own_bars, part):
+        view = dict(own_bars)
+        view["acc_empty"] = lead["acc_empty"]
+        return (owner_warp(view, segs, MT, slots, part) if own
+                else slice_warp(view, segs, MT, slots, part))
+
+    roles = [producer_of(lead), producer_of(follow), mma(mma_view, segs, MT, ST, XS, slots)]
+    for bars in (lead, follow):
+        for w in range(8):
+            roles.append(epi_of(bars, w >> 2))
+    live = list(roles)
+
+    def state():
+        return [(b.phase, b.pending) for B in (lead, follow) for v in B.values() for b in v]
+
+    while live:
+        before, finished = state(), False
+        for r in list(live):
+            try:
+                next(r)
+            except StopIteration:
+                live.remove(r)
+                finished = True
+        if not finished and state() == before:
+            raise AssertionError("deadlock: no role can make progress")
+
+
+PAIR_CONFIGS = [
+    dict(MT=1, NC=128, ST=2, XS=1, own=False),   # 256 < D <= 384
+    dict(MT=2, NC=256, ST=8, XS=1, own=True),    # D <= 64 (pairs opted in)
+    dict(MT=2, NC=256, ST=4, XS=1, own=False),   # D <= 128 (pairs opted in)
+    dict(MT=1, NC=256, ST=2, XS=1, own=False),   # D <= 256 (pairs opted in)
+]
+
+
+@pytest.mark.parametrize("cfg", PAIR_CONFIGS, ids=lambda c: "-".join(f"{k}{v}" for k, v in c.items()))
+@pytest.mark.parametrize("total_tiles,nchunks,units", [(7, 1, 3), (9, 4, 4), (20, 3, 6), (5, 8, 3)])
+def test_pairs_no_deadlock(cfg, total_tiles, nchunks, units):
+    for unit in range(min(units, 4)):  # pairs run whole tiles only (no split mode)
+        run_pair([(t, 0, nchunks) for t in range(unit, total_tiles, units)], nchunks=nchunks,
+                 **cfg)
