@@ -248,6 +248,8 @@ def batch_kmeans_Euclid_sharded(
     B, n_local, D = x_local.shape
     K = int(n_clusters)
     world = dist.get_world_size(group)
+    if world > 1:
+        _check_shards(x_local, K, shard, group)
 
     if init_centroids is None:
         if shard == "N":
@@ -317,6 +319,26 @@ def batch_kmeans_Euclid_sharded(
             labels = _all_gather_var(labels, dim=0, group=group)
             cur = _all_gather_var(cur, dim=0, group=group)
     return labels, cur, n_iters_run
+
+
+def _check_shards(x_local: torch.Tensor, K: int, shard: str, group) -> None:
+    """Every rank must agree on K, D, the shard mode and the unsharded extent (B for
+    ``shard="N"``, N for ``shard="B"``); a mismatch raises ValueError on every rank (each
+    rank sees all ranks' shapes) instead of a hang or a garbled all-reduce."""
+    world = dist.get_world_size(group)
+    B, N, D = (int(v) for v in x_local.shape)
+    mine = torch.tensor([B, N, D, K, 0 if shard == "N" else 1], device=x_local.device,
+                        dtype=torch.int64)
+    alls = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(alls, mine, group=group)
+    rows = [tuple(int(v) for v in t.tolist()) for t in alls]
+    keep = (0, 2, 3, 4) if shard == "N" else (1, 2, 3, 4)  # what must match
+    ref = rows[0]
+    for r, row in enumerate(rows):
+        if any(row[i] != ref[i] for i in keep):
+            raise ValueError(
+                f"sharded K-Means: rank {r} has (B, N, D, K, shard) = {row}, rank 0 has {ref}; "
+                f"ranks must agree on " + ("B, D and K" if shard == "N" else "N, D and K"))
 
 
 def _all_gather_var(t: torch.Tensor, dim: int, group) -> torch.Tensor:

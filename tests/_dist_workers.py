@@ -104,3 +104,45 @@ def failing_rank(rank: int, world: int, port: int, out_path: str) -> None:
     with open(out_path, "w") as f:
         f.write(status)
     os._exit(0)
+
+
+def mismatched_rank(rank: int, world: int, port: int, out_path: str) -> None:
+    """Rank 1 holds rows of another width: every rank must raise, none may hang."""
+    from flash_kmeans_cuda.distributed import batch_kmeans_Euclid_sharded
+
+    _init(rank, world, port, 20.0)
+    x = torch.randn(1, 100, 4 if rank == 0 else 5)
+    try:
+        batch_kmeans_Euclid_sharded(x, 4, max_iters=3, state_factory=OracleState)
+        status = "no-error"
+    except ValueError as e:
+        status = "error:ValueError:" + str(e)
+    except Exception as e:  # noqa: BLE001
+        status = "error:" + type(e).__name__
+    with open(f"{out_path}.{rank}", "w") as f:
+        f.write(status)
+    os._exit(0)
+
+
+def stalled_rank(rank: int, world: int, port: int, out_path: str) -> None:
+    """Rank 1 stalls longer than the process-group timeout before its first collective:
+    rank 0's collective must end with an error after the timeout, not hang."""
+    import time
+
+    from flash_kmeans_cuda.distributed import batch_kmeans_Euclid_sharded
+
+    _init(rank, world, port, 3.0)
+    x = torch.randn(1, 100, 4)
+    if rank == 1:
+        time.sleep(20.0)
+        os._exit(0)
+    t0 = time.time()
+    try:
+        batch_kmeans_Euclid_sharded(x, 4, max_iters=3, state_factory=OracleState)
+        status = "no-error"
+    except Exception as e:  # noqa: BLE001
+        status = f"error:{type(e).__name__}:{time.time() - t0:.1f}"
+    with open(out_path, "w") as f:
+        f.write(status)
+    os._exit(0)
+

@@ -58,3 +58,39 @@ def test_dead_rank_surfaces_as_error(tmp_path):
     assert os.path.exists(out), "rank 0 neither finished nor reported"
     assert open(out).read().startswith("error:")
     assert time.time() - t0 < 120
+
+
+def _run(fn, args, deadline_s):
+    t0 = time.time()
+    ctx = mp.start_processes(fn, args=args, nprocs=2, start_method="spawn", join=False)
+    while time.time() - t0 < deadline_s and any(p.is_alive() for p in ctx.processes):
+        time.sleep(0.2)
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    return time.time() - t0
+
+
+def test_mismatched_shards_raise_on_every_rank(tmp_path):
+    from _dist_workers import mismatched_rank
+
+    out = str(tmp_path / "status")
+    elapsed = _run(mismatched_rank, (2, _port(), out), 90)
+    for r in range(2):
+        status = open(f"{out}.{r}").read()
+        assert status.startswith("error:ValueError"), status
+        assert "rank 1" in status
+    assert elapsed < 90
+
+
+def test_stalled_rank_times_out_instead_of_hanging(tmp_path):
+    from _dist_workers import stalled_rank
+
+    out = str(tmp_path / "status.txt")
+    elapsed = _run(stalled_rank, (2, _port(), out), 90)
+    status = open(out).read()
+    assert status.startswith("error:"), status
+    waited = float(status.rsplit(":", 1)[1])
+    assert 2.0 <= waited < 20.0  # the 3 s process-group timeout, not the peer's 20 s stall
+    assert elapsed < 90
+
