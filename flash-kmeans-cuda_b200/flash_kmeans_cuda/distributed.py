@@ -31,6 +31,8 @@ from typing import Callable, Optional, Tuple
 import torch
 import torch.distributed as dist
 
+from ._trace import nvtx
+
 
 def shard_bounds(total: int, world: int, rank: int) -> Tuple[int, int]:
     """Contiguous [begin, end) of ``total`` items for ``rank`` (sizes differ by <= 1)."""
@@ -69,8 +71,9 @@ def allreduce_sums_counts(sums: torch.Tensor, counts: torch.Tensor, group=None) 
     """Sum ``sums`` (fp32) and ``counts`` (int32) over the group (two all-reduces:
     the collectives cannot be grouped across dtypes, and counts stay int32, exact
     for any point count below 2**31)."""
-    dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
-    dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
+    with nvtx("fkc.allreduce"):
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM, group=group)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM, group=group)
 
 
 def multimem_enabled() -> bool:

@@ -21,6 +21,7 @@ from typing import Optional, Tuple
 import torch
 
 from . import _C, _lib
+from ._trace import nvtx
 from ._lib import lib
 
 
@@ -86,13 +87,13 @@ class LloydState:
 
     def local(self, c: torch.Tensor) -> None:
         """Assign + counting-sort update of this state's x against ``c``."""
-        with torch.cuda.device(self.device):
+        with nvtx("fkc.local"), torch.cuda.device(self.device):
             _lib.check(lib.fkc_lloyd_local(self.x.data_ptr(), c.data_ptr(), self.ids.data_ptr(),
                                            self.sums.data_ptr(), self.counts.data_ptr(),
                                            *self._dims()), "fkc_lloyd_local")
 
     def finalize(self, old: torch.Tensor, new: torch.Tensor, want_shift: bool) -> None:
-        with torch.cuda.device(self.device):
+        with nvtx("fkc.finalize"), torch.cuda.device(self.device):
             _lib.check(lib.fkc_lloyd_finalize(self.sums.data_ptr(), self.counts.data_ptr(),
                                               old.data_ptr(), new.data_ptr(),
                                               self.shift.data_ptr() if want_shift else None,
@@ -105,7 +106,7 @@ class LloydState:
         """
         self._check_c(c)
         n = torch.zeros((1,), dtype=torch.int32, device=self.device)
-        with torch.cuda.device(self.device):
+        with nvtx("fkc.run"), torch.cuda.device(self.device):
             _lib.check(lib.fkc_lloyd_run(self.x.data_ptr(), c.data_ptr(), self.ids.data_ptr(),
                                          self.sums.data_ptr(), self.counts.data_ptr(),
                                          self.shift.data_ptr(), n.data_ptr(), int(max_iters),
@@ -114,7 +115,7 @@ class LloydState:
 
     def step(self, old: torch.Tensor, new: torch.Tensor, want_shift: bool) -> None:
         """One full Lloyd iteration: ids/sums/counts from ``old``, centroids into ``new``."""
-        with torch.cuda.device(self.device):
+        with nvtx("fkc.step"), torch.cuda.device(self.device):
             _lib.check(lib.fkc_lloyd_iter(self.x.data_ptr(), old.data_ptr(), new.data_ptr(),
                                           self.ids.data_ptr(), self.sums.data_ptr(),
                                           self.counts.data_ptr(),

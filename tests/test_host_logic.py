@@ -69,3 +69,17 @@ def test_import_fails_loudly_without_library(tmp_path):
             "import flash_kmeans_cuda")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True)
     assert r.returncode != 0 and "ImportError" in r.stderr
+
+
+def test_nvtx_ranges_are_noops_unless_enabled(monkeypatch):
+    from flash_kmeans_cuda import _trace
+
+    monkeypatch.setattr(_trace, "ENABLED", False)
+    with _trace.nvtx("x"):
+        pass
+    monkeypatch.setattr(_trace, "ENABLED", True)
+    with _trace.nvtx("y"):  # pushes and pops a range (works without a GPU)
+        pass
+    with pytest.raises(ZeroDivisionError):
+        with _trace.nvtx("z"):
+            1 / 0  # the range is popped on the way out
