@@ -11,25 +11,30 @@
 // for the tensor-core path.
 //
 // How. The scratch (the per-point and per-centroid norm slices the tensor-core
-// kernel reads, 32 bytes per row) lives in a file-scope __device__ array of
-// FKC_ASSIGN_NOALLOC_SCRATCH_BYTES (32 MiB). The CUDA runtime places it when
-// this file's module is loaded on a device; nothing here calls cudaMalloc,
-// cudaFree or an allocating library routine. The first call on each device
-// looks up the array's address on that device with cudaGetSymbolAddress (with
-// the device current) and caches it. The call then runs exactly the fkc_assign
-// code path with the array as its workspace.
+// kernel reads, 32 bytes per row; for fp32 also the split bf16 operand rows)
+// lives in a file-scope __device__ array of FKC_ASSIGN_NOALLOC_SCRATCH_BYTES
+// (32 MiB). The CUDA runtime places it when this file's module is loaded on a
+// device; nothing here calls cudaMalloc, cudaFree or an allocating library
+// routine. In host code the array's name is only a host-side stand-in, so
+// every call looks up the array's address on the current device with
+// cudaGetSymbolAddress (a host-side query that allocates nothing) and passes
+// that address on. Looking it up per call rather than caching it keeps the
+// address right when the device's context is torn down and created again
+// (cudaDeviceReset, a primary-context reset), after which the module is
+// loaded anew and the array may sit elsewhere. The first call on a device
+// also loads the module there (the runtime loads modules lazily), so that
+// first call should come before any stream capture. The call then runs
+// exactly the fkc_assign code path with the array as its workspace.
 //
 // Sharing. Every call on a device uses the same array. Nothing in it has to
-// start at zero: each call writes both norm slices in full before the
-// assignment kernel reads them, and the kernel's tensor maps end at N and K,
-// so it never reads rows of the array beyond this call's slices. Calls that
-// overlap on the GPU (different streams with no ordering between them, or
-// different host threads) race on the array; order them on one stream or with
-// events. Calls on different devices use different instances of the array.
+// start at zero: each call writes both norm slices (and the split rows) in
+// full before the assignment kernel reads them, and the kernel's tensor maps
+// end at N and K, so it never reads rows of the array beyond this call's
+// slices. The array keeps whatever the last call wrote. Calls that overlap on
+// the GPU (different streams with no ordering between them, or different host
+// threads) race on the array; order them on one stream or with events. Calls
+// on different devices use different instances of the array.
 #include <cuda_runtime.h>
-
-#include <array>
-#include <mutex>
 
 #include "fkc_internal.h"
 
@@ -40,12 +45,7 @@ static __device__ __align__(256) uint8_t g_fkc_noalloc_scratch[FKC_ASSIGN_NOALLO
 namespace fkc {
 namespace {
 
-constexpr int kMaxNoallocDevices = 64;
-std::mutex g_noalloc_mu;
-std::array<void*, kMaxNoallocDevices> g_noalloc_ptr{};
-
-// Address of the scratch array on the current device (looked up once per
-// device, with that device current).
+// Device address of the scratch array in the current context.
 int noalloc_scratch(void** out) {
   int dev = -1;
   const cudaError_t de = cudaGetDevice(&dev);
@@ -53,20 +53,14 @@ int noalloc_scratch(void** out) {
     cudaGetLastError();
     return set_error(FKC_EUNSUPPORTED, "no CUDA device: %s", cudaGetErrorString(de));
   }
-  if (dev < 0 || dev >= kMaxNoallocDevices)
-    return set_error(FKC_EUNSUPPORTED, "device index %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_fkc_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      cudaGetLastError();
-      return set_error(FKC_ECUDA, "fkc_assign_noalloc: scratch lookup on device %d failed: %s",
-                       dev, cudaGetErrorString(e));
-    }
-    g_noalloc_ptr[dev] = p;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_fkc_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    cudaGetLastError();
+    return set_error(FKC_ECUDA, "fkc_assign_noalloc: scratch lookup on device %d failed: %s",
+                     dev, cudaGetErrorString(e));
   }
-  *out = g_noalloc_ptr[dev];
+  *out = p;
   return FKC_OK;
 }
 
@@ -78,11 +72,16 @@ extern "C" FKC_CAPI_EXPORT int fkc_assign_noalloc(const void* x, const void* cen
                                                   int32_t* ids, int64_t B, int64_t N, int64_t K,
                                                   int64_t D, int dtype, fkc_stream_t stream) {
   fkc::clear_error();
-  // The size check comes before any CUDA call. Shapes that do not take the
-  // tensor-core path need no scratch (0 here); invalid shapes also give 0 and
-  // are reported by fkc_assign's own argument checks.
-  size_t need = fkc_assign_workspace_size(B, N, K, D, dtype);
-  // fp32 beyond the scratch: the CUDA-core kernel, which needs no scratch.
+  // The size check comes before any CUDA call. A call that fkc_assign would
+  // route to the CUDA-core kernel needs no scratch (0 here): a shape or dtype
+  // outside the tensor-core path, FKC_ASSIGN_FORCE_SAFE=1, or x / centroids
+  // not 16-byte aligned. Invalid shapes also give 0 and are reported by
+  // fkc_assign's own argument checks.
+  size_t need = fkc::assign_may_use_tc_host(x, centroids, D, dtype)
+                    ? fkc_assign_workspace_size(B, N, K, D, dtype)
+                    : 0;
+  // fp32 beyond the scratch: fkc_assign keeps the CUDA-core kernel when the
+  // workspace cannot hold the split operand rows, so no scratch is needed.
   if (dtype == FKC_DTYPE_F32 && need > static_cast<size_t>(FKC_ASSIGN_NOALLOC_SCRATCH_BYTES))
     need = 0;
   if (need > static_cast<size_t>(FKC_ASSIGN_NOALLOC_SCRATCH_BYTES))

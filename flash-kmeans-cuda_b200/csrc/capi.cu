@@ -158,6 +158,14 @@ bool use_tc(const void* x, const void* c, int64_t D, int dtype) {
          assign_tc_supported(split ? 3 * D : D, split ? FKC_DTYPE_BF16 : dtype);
 }
 
+}  // namespace
+
+bool assign_may_use_tc_host(const void* x, const void* c, int64_t D, int dtype) {
+  return tc_shape_ok(D, dtype) && !force_safe_path() && aligned16(x) && aligned16(c);
+}
+
+namespace {
+
 // Operand rows of the split-fp32 path: x3 (B, N, 3D) and c3 (B, K, 3D) bf16.
 size_t split_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   if (!split_f32(D, dtype)) return 0;

@@ -75,6 +75,11 @@ void count_launches(int n);
 // True when the tcgen05 assignment kernel handles this shape/dtype on the
 // current device.
 bool assign_tc_supported(int64_t D, int dtype);
+// The host-only part of fkc_assign's route choice (no CUDA call): false when
+// the call certainly takes the CUDA-core kernel, which needs no workspace
+// (shape/dtype outside the tensor-core path, FKC_ASSIGN_FORCE_SAFE=1, or x /
+// centroids not 16-byte aligned).
+bool assign_may_use_tc_host(const void* x, const void* c, int64_t D, int dtype);
 
 // Row-norm extension rows for the tcgen05 path: aext[b,n,:] = {h1,h2,h3,1,1,1,0...}
 // with h1+h2+h3 = -0.5*||x[b,n]||^2 split over three bf16 values.

@@ -1,4 +1,5 @@
-"""Python op wrappers with the reference's signatures (``flash_kmeans_cuda/ops.py:30-129``).
+"""Python op wrappers with the reference's names, arguments and errors
+(``flash_kmeans_cuda/ops.py:30-129``).
 
 ``centroid_update_sorted`` keeps its name and arguments but no longer calls
 ``torch.sort`` + ``gather``: labels go through the library's counting sort
@@ -17,11 +18,11 @@ from ._lib import lib
 
 
 def _ensure_contig(t: torch.Tensor, name: str) -> torch.Tensor:
-    if not t.is_cuda:
-        raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
-    if not t.is_contiguous():
-        return t.contiguous()
-    return t
+    # Error contract of the reference (ops.py:22-27): ValueError naming the
+    # argument when it is not on a CUDA device; a contiguous copy otherwise.
+    if t.is_cuda:
+        return t if t.is_contiguous() else t.contiguous()
+    raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
 
 
 def euclid_assign(
@@ -31,25 +32,21 @@ def euclid_assign(
     c_sq: Optional[torch.Tensor] = None,
     out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """Assign each point to its nearest centroid (Euclidean); ties -> lowest index.
+    """Label of the nearest centroid for every point; equal distances go to the
+    lower centroid index.
 
-    Args:
-        x: (B, N, D) fp16/bf16/fp32, CUDA.
-        centroids: (B, K, D) same dtype as x.
-        x_sq: (B, N) fp32 ||x||^2 (read only by the fp32 / odd-D kernel).
-        c_sq: (B, K) fp32 ||c||^2; computed from ``centroids`` if None.
-        out: optional (B, N) int32 output buffer.
-
-    Returns:
-        cluster_ids: (B, N) int32.
+    ``x`` is (B, N, D) and ``centroids`` (B, K, D), both CUDA tensors of one
+    dtype (float16, bfloat16 or float32). ``x_sq`` (B, N) and ``c_sq`` (B, K)
+    are float32 squared row norms; the tensor-core kernel computes its own norms
+    and ignores both, the CUDA-core kernel (float32, odd D) reads them, and a
+    missing ``c_sq`` is computed here. ``out``, when given, is the (B, N) int32
+    tensor the labels are written into and returned; otherwise a new one is.
     """
-    x = _ensure_contig(x, "x")
-    centroids = _ensure_contig(centroids, "centroids")
-    x_sq = _ensure_contig(x_sq, "x_sq").to(torch.float32)
+    xs = [_ensure_contig(t, n) for t, n in ((x, "x"), (centroids, "centroids"), (x_sq, "x_sq"))]
+    x, centroids, x_sq = xs[0], xs[1], xs[2].float()
     if c_sq is None:
-        c_sq = (centroids.float() ** 2).sum(dim=-1)
-    c_sq = _ensure_contig(c_sq, "c_sq").to(torch.float32)
-    return _C.euclid_assign(x, centroids, x_sq, c_sq, out)
+        c_sq = centroids.float().square().sum(-1)
+    return _C.euclid_assign(x, centroids, x_sq, _ensure_contig(c_sq, "c_sq").float(), out)
 
 
 def centroid_update_sorted(
@@ -96,13 +93,9 @@ def centroid_finalize(
     old_centroids: torch.Tensor,
     out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """new[b,k] = sums[b,k] / counts[b,k] if counts > 0 else old_centroids[b,k].
-
-    Casts back to old_centroids.dtype.
-    """
-    return _C.centroid_finalize(
-        centroid_sums.contiguous(),
-        centroid_counts.contiguous(),
-        old_centroids.contiguous(),
-        out,
-    )
+    """Mean of every non-empty cluster (sums / counts, computed in fp32) in the
+    dtype of ``old_centroids``; an empty cluster keeps its old centroid. Written
+    into ``out`` when it is given."""
+    args = [t if t.is_contiguous() else t.contiguous()
+            for t in (centroid_sums, centroid_counts, old_centroids)]
+    return _C.centroid_finalize(*args, out)

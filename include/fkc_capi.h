@@ -114,12 +114,16 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
  * pipelines that cannot take cudaFree's device-wide synchronisation.
  *   Same arguments, results and errors as fkc_assign minus the workspace.
  *   Scratch: a static device array of FKC_ASSIGN_NOALLOC_SCRATCH_BYTES per
- *   device (32 MiB), needed on the tensor-core path only. A call needing more
- *   than that, i.e. fkc_assign_workspace_size() > the limit (about
- *   B*N + B*K > 1,048,000 rows), returns FKC_EWORKSPACE with a message and
- *   launches nothing.
- *   The first call on each device looks up the scratch address on that device
- *   (a set-up step): make that first call before any stream capture.
+ *   device (32 MiB), needed on the tensor-core path only. A tensor-core call
+ *   needing more than that, i.e. fkc_assign_workspace_size() > the limit
+ *   (about B*N + B*K > 1,048,000 rows), returns FKC_EWORKSPACE with a message
+ *   and launches nothing. Calls that take the CUDA-core kernel (fp32 beyond
+ *   the scratch, odd D, FKC_ASSIGN_FORCE_SAFE=1, x or centroids not 16-byte
+ *   aligned) need no scratch and have no limit.
+ *   Every call looks up the scratch address on the current device (a host-side
+ *   query; the address stays right across a device reset). The first call on
+ *   a device also loads this library's device code there (a set-up step): make
+ *   that first call before any stream capture.
  *   All calls on a device share the scratch: calls that overlap on the GPU
  *   (unordered streams, concurrent host threads) race. Order them.
  *   Allocates nothing: no cudaMalloc, cudaFree or allocating library call.

@@ -10,7 +10,11 @@
 #                        built here: nanobind is not installed).
 # Test infrastructure only (see oracle/lloyd.py for the rule on who may use it).
 set -euo pipefail
-REF=${FKC_REFERENCE_ROOT:-/root/reference}
+if [ -z "${FKC_REFERENCE_ROOT:-}" ]; then
+  echo "FKC_REFERENCE_ROOT is not set: point it at a checkout of the reference to build oracle/_ref" >&2
+  exit 2
+fi
+REF=$FKC_REFERENCE_ROOT
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT=$HERE/_ref
 CSRC=$REF/flash_kmeans_cuda/csrc

@@ -107,13 +107,58 @@ def test_noalloc_rejects_oversize_before_any_cuda_call():
     L = _lib.lib
     limit = 32 * 1024 * 1024
     assert L.fkc_assign_workspace_size(1, limit // 32 - 8192, 8192, 64, 0) == limit
-    st = L.fkc_assign_noalloc(1, 1, None, None, 1, 1, limit // 32 - 8192 + 1, 8192, 64, 0, None)
+    # 16-byte aligned stand-in pointers and a null ids: nothing could be launched either way
+    st = L.fkc_assign_noalloc(4096, 8192, None, None, None, 1, limit // 32 - 8192 + 1, 8192, 64,
+                              0, None)
     assert st == -5 and "static scratch" in _lib.last_error()
+    # exactly at the limit: past the size check (no device here: -3; with one: null ids, -1)
+    st = L.fkc_assign_noalloc(4096, 8192, None, None, None, 1, limit // 32 - 8192, 8192, 64,
+                              0, None)
+    assert st in (-1, -3) and "static scratch" not in _lib.last_error()
     # fp32 beyond the scratch falls back to the CUDA-core kernel: the limit does not apply
     st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 64, 2, None)
     assert st == -1 and "non-null" in _lib.last_error()
     st = L.fkc_assign_noalloc(None, 1, None, None, 1, 1, 1 << 24, 8192, 72, 2, None)
     assert st == -1 and "non-null" in _lib.last_error()
+
+
+def test_noalloc_limit_skipped_for_cuda_core_route():
+    """A call that fkc_assign routes to the CUDA-core kernel (x or centroids not 16-byte
+    aligned) needs no scratch, so the size limit does not apply: the oversize call gets
+    past it to fkc_assign's own argument checks (null ids here; nothing is launched)."""
+    from flash_kmeans_cuda import _lib
+
+    L = _lib.lib
+    n = 1 << 24  # far beyond the 32 MiB scratch at fp16, D=64
+    st = L.fkc_assign_noalloc(16 + 2, 4096, None, None, None, 1, n, 8192, 64, 0, None)
+    assert st == -1 and "non-null" in _lib.last_error()
+    st = L.fkc_assign_noalloc(4096, 16 + 8, None, None, None, 1, n, 8192, 64, 0, None)
+    assert st == -1 and "non-null" in _lib.last_error()
+    # 16-byte aligned: the tensor-core route, whose scratch need is checked first
+    st = L.fkc_assign_noalloc(4096, 8192, None, None, None, 1, n, 8192, 64, 0, None)
+    assert st == -5 and "static scratch" in _lib.last_error()
+
+
+def test_noalloc_limit_skipped_when_forced_safe():
+    """FKC_ASSIGN_FORCE_SAFE=1 (read once per process) routes every call to the CUDA-core
+    kernel: no scratch, no limit (checked in a child process)."""
+    import os
+    import subprocess
+    import sys
+
+    pkg = str(ROOT / "flash-kmeans-cuda_b200")
+    code = (
+        "import sys; sys.path[:0] = [%r, %r]\n"
+        "from flash_kmeans_cuda import _lib\n"
+        "st = _lib.lib.fkc_assign_noalloc(4096, 8192, None, None, None, 1, 1 << 24, 8192, 64,"
+        " 0, None)\n"
+        "print(st, _lib.last_error())\n" % (pkg, str(ROOT)))
+    env = dict(os.environ, FKC_ASSIGN_FORCE_SAFE="1")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr
+    st, msg = out.stdout.strip().split(" ", 1)
+    assert int(st) == -1 and "non-null" in msg
 
 
 def test_selftest_timeout_checked_before_any_cuda_call():

@@ -1,10 +1,13 @@
 """fkc_assign_noalloc (static-scratch assignment) against fkc_assign, through the C-ABI.
 
-Collected last on purpose (file name): the entry point must give the same
-labels whether it is the first CUDA work of a fresh process or runs after every
-other test. Each call's labels must be identical to fkc_assign's on the same
-inputs, for two calls in a row whose shapes differ (the second call reuses the
-scratch the first one wrote).
+The entry point exists for callers that cannot allocate device memory (FFI
+bindings that only receive device pointers, hosts whose device memory a
+pooling allocator owns, pipelines that cannot take cudaFree's device-wide
+sync). Its labels must be identical to fkc_assign's on the same inputs:
+for two calls in a row whose shapes differ (the second call reuses the
+scratch the first one wrote), after every other test of the suite (this file
+is collected last), and as the library's first CUDA work in a fresh process
+(a child process).
 """
 
 from __future__ import annotations
@@ -82,6 +85,10 @@ def test_noalloc_allocates_nothing_after_setup(cuda_device):
     out = torch.full_like(want, -1)
     _assign_noalloc(x, c, out)  # set-up (first call on this device) already done or done here
     torch.cuda.synchronize()
+    # What this process holds through torch's allocator must not move at all; the
+    # device-wide free figure also counts other processes, so it gets a loose bound
+    # (far below the 32 MiB a workspace of this shape would take).
+    reserved0, allocated0 = torch.cuda.memory_reserved(), torch.cuda.memory_allocated()
     free0, _ = torch.cuda.mem_get_info()
     for _ in range(3):
         out.fill_(-1)
@@ -89,7 +96,52 @@ def test_noalloc_allocates_nothing_after_setup(cuda_device):
     torch.cuda.synchronize()
     free1, _ = torch.cuda.mem_get_info()
     assert torch.equal(out, want)
-    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    assert torch.cuda.memory_reserved() == reserved0
+    assert torch.cuda.memory_allocated() == allocated0
+    assert abs(free0 - free1) < (1 << 20), f"device free memory moved by {free0 - free1} bytes"
+
+
+_FRESH_CHILD = r"""
+import sys
+sys.path[:0] = [{pkg!r}, {root!r}, {tests!r}]
+import torch
+from _data import iid, subset_init
+from flash_kmeans_cuda import _lib as L
+assert L.lib.fkc_kernel_launches() == 0
+x = iid(1, 30000, 128, seed=61, dtype="float16").cuda()
+c = subset_init(x.cpu(), 300, seed=62).cuda()
+st = torch.cuda.current_stream().cuda_stream
+got = torch.full((1, 30000), -1, dtype=torch.int32, device="cuda")
+# the library's first CUDA work in this process: module load + scratch lookup + launch
+L.check(L.lib.fkc_assign_noalloc(x.data_ptr(), c.data_ptr(), None, None, got.data_ptr(), 1,
+                                 30000, 300, 128, 0, st), "fkc_assign_noalloc")
+need = L.lib.fkc_assign_workspace_size(1, 30000, 300, 128, 0)
+ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+want = torch.full_like(got, -1)
+L.check(L.lib.fkc_assign(x.data_ptr(), c.data_ptr(), None, None, want.data_ptr(), 1, 30000, 300,
+                         128, 0, ws.data_ptr(), need, st), "fkc_assign")
+torch.cuda.synchronize()
+L.device_status()
+assert torch.equal(got, want), "labels differ"
+print("fresh-ok", L.lib.fkc_kernel_launches())
+"""
+
+
+def test_noalloc_first_call_in_fresh_process(cuda_device):
+    """fkc_assign_noalloc as the library's first CUDA work in a new process (the set-up
+    path: lazy module load and scratch lookup) gives fkc_assign's labels."""
+    import os
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = _FRESH_CHILD.format(pkg=os.path.join(root, "flash-kmeans-cuda_b200"), root=root,
+                               tests=here)
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         timeout=600)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-4000:]
+    assert "fresh-ok" in out.stdout
 
 
 def test_noalloc_size_limit(cuda_device):
@@ -115,10 +167,27 @@ def test_noalloc_size_limit(cuda_device):
 
 
 def test_noalloc_cuda_core_path(cuda_device):
-    """fp32 and odd D take the CUDA-core kernel, which needs no scratch at all."""
-    for dt, D in (("float32", 64), ("float16", 33)):
+    """fp32 at D > 128 and odd D take the CUDA-core kernel, which needs no scratch; fp32 at
+    D <= 128 takes the split-bf16 tensor-core route through the scratch. All equal
+    fkc_assign's labels."""
+    for dt, D in (("float32", 64), ("float32", 144), ("float16", 33)):
         x, c = _inputs(1, 4000, 100, D, dt, 51)
         got = _assign_noalloc(x, c)
         want = _assign_ws(x, c)
         torch.cuda.synchronize()
         assert torch.equal(got, want), f"{dt} D={D}"
+
+
+def test_noalloc_unaligned_input_has_no_limit(cuda_device):
+    """x not 16-byte aligned: fkc_assign takes the CUDA-core kernel, so the no-alloc call
+    needs no scratch and has no size limit (1.1 M points would need 35 MB of tensor-core
+    scratch); labels equal fkc_assign's on the same (unaligned) view."""
+    n = 1_100_000
+    base = iid(1, n * 64 + 1, 1, seed=57, dtype="float16").cuda().view(-1)
+    x = base[1:].view(1, n, 64)  # starts 2 bytes past an aligned address
+    assert x.data_ptr() % 16 != 0
+    c = subset_init(x.cpu(), 50, seed=58).cuda()
+    got = _assign_noalloc(x, c)
+    want = _assign_ws(x, c)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
