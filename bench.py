@@ -18,9 +18,20 @@ distributions, generated on the device):
 Extra keys: ``roofline`` for the assignment kernel (tensor-bound, against the
 measured bf16/fp16 dense peak), ``update`` (HBM-bound, GB/s), ``e2e`` (the same
 metric through ``batch_kmeans_Euclid`` with host-resident inputs copied in and
-results copied out inside the timed region), ``cpu_baseline`` (multi-threaded
-CPU Lloyd loop on a bounded sample, scaled to the whole workload), ``clocks``
-(nvidia-smi samples during the timed region) and ``gpu_launches``.
+results copied out inside the timed region), ``e2e_device`` (whole
+``batch_kmeans_Euclid`` calls on device-resident x, the reference's own
+end-to-end definition), ``parity`` (labels of the last timed step on a fixed
+row subset against a float64 assignment, counts against the label histogram),
+``per_rank`` (N > 1: each rank's local step, reduction and barrier times),
+``cpu_baseline`` (multi-threaded CPU Lloyd loop on a bounded sample, scaled to
+the whole workload), ``cpu_baseline_c1`` (BASELINE config 1 in full on the host
+cores), ``clocks`` (nvidia-smi samples during the timed region) and
+``gpu_launches``.
+
+``--impl reference`` times the reference's loop on the host cores (its CPU
+port on a sample of the workload's own distribution) and adds
+``reference_gpu``: the reference's own CUDA kernels, built from its sources
+under oracle/_ref, on the whole workload on GPU 0.
 """
 
 from __future__ import annotations
@@ -63,9 +74,14 @@ def log(*a):
 
 
 # --------------------------------------------------------------------------- data
-def make_data(w: dict, device, seed: int = 0):
-    """Full (B, N, D) points and (B, K, D) initial centroids (seeded subset of the points)."""
+def make_data(w: dict, device, seed: int = 0, n_rows=None, dtype=None):
+    """(B, N, D) points and (B, K, D) initial centroids (seeded subset of the points).
+
+    ``n_rows`` draws that many points per batch element from the same distribution
+    (a sample, for the CPU timings); ``dtype`` overrides the workload's dtype."""
     B, N, K, D = w["B"], w["N"], w["K"], w["D"]
+    if n_rows is not None:
+        N = int(n_rows)
     g = torch.Generator(device=device).manual_seed(seed)
     xs = []
     for b in range(B):
@@ -82,7 +98,7 @@ def make_data(w: dict, device, seed: int = 0):
                 lab = torch.randint(0, nc, (N,), generator=g, device=device)
             xb = centres[lab]
             xb.add_(torch.randn((N, D), generator=g, device=device))
-        xs.append(xb.to(TDT[w["dtype"]]))
+        xs.append(xb.to(dtype or TDT[w["dtype"]]))
         del xb
     x = torch.stack(xs)
     del xs
@@ -222,23 +238,79 @@ def cpu_baseline(w: dict, workload: str) -> dict:
                        f"oracle/cpu_lloyd.py), median of 3, scaled by {scale:.1f}x")}
 
 
-def run_reference_gpu(args, w: dict) -> None:
-    """The reference's own CUDA kernels (oracle/_ref, built from its sources) on the
-    same workload, one GPU: a step is one Lloyd iteration of the reference's loop
-    (c_sq, fkc::euclid_assign, torch.sort + sorted/indexed accumulate, finalize)."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+def cpu_baseline_c1() -> dict:
+    """BASELINE config 1 in full on the host cores: B=1, N=32768, K=256, D=128 fp32, iid
+    N(0, 1) from seed 0, K rows of a seeded randperm as initial centroids, 10 iterations,
+    median of 3 (the CPU PyTorch Lloyd loop of oracle/cpu_lloyd.py)."""
+    from oracle.cpu_lloyd import time_lloyd_cpu
+
+    r = time_lloyd_cpu(1, 32768, 256, 128, iters=10, seed=0, repeats=3)
+    return {"value": r["ms_per_iter"], "unit": "ms/iter", "cores": r["threads"], "kind": "port",
+            "sample": "c1 in full: B=1 N=32768 K=256 D=128 fp32 iid, 10 iterations, median of 3"}
+
+
+def sample_parity(x: torch.Tensor, c: torch.Tensor, ids: torch.Tensor, counts: torch.Tensor,
+                  max_rows: int = 8192) -> dict:
+    """Labels of a fixed, evenly strided subset of rows against a float64 restatement
+    of the assignment (argmin_k ||x||^2 + ||c||^2 - 2 x.c, ties to the lowest index)
+    computed on the device with torch (no code of this library), and the counts
+    against the histogram of all labels (exact)."""
+    B, N, D = x.shape
+    K = c.shape[1]
+    total = B * N
+    n_s = int(min(total, max_rows, max(256, (1 << 27) // K)))
+    flat = torch.linspace(0, total - 1, n_s, device=x.device).round().to(torch.int64).unique()
+    bb, nn = flat // N, flat % N
+    mismatch, agree, near = 0, 0, 0
+    for b in bb.unique().tolist():
+        sel = nn[bb == b]
+        xr = x[b, sel].to(torch.float64)
+        cb = c[b].to(torch.float64)
+        x_sq = (xr * xr).sum(-1)
+        dist = x_sq[:, None] + (cb * cb).sum(-1)[None, :] - 2.0 * (xr @ cb.T)
+        best, exact = dist.min(dim=1)  # first occurrence: the lowest index on ties
+        if K > 1:
+            dist[torch.arange(dist.shape[0], device=x.device), exact] = float("inf")
+            gap_ok = (dist.min(dim=1).values - best) > 1e-3 * x_sq
+        else:
+            gap_ok = torch.ones_like(best, dtype=torch.bool)
+        got = ids[b, sel].to(torch.int64)
+        mismatch += int(((got != exact) & gap_ok).sum())
+        agree += int((got == exact).sum())
+        near += int((~gap_ok).sum())
+        del dist
+    hist_ok = all(torch.equal(torch.bincount(ids[b].to(torch.int64), minlength=K).to(torch.int32),
+                              counts[b]) for b in range(B))
+    return {"rows": int(flat.numel()), "labels_above_gap_mismatch": mismatch,
+            "agree": agree / max(1, int(flat.numel())), "near_tie_rows": near,
+            "counts_exact": bool(hist_ok)}
+
+
+def reduce_parity(p: dict, device) -> dict:
+    """Sums the per-rank parity counts (every rank calls it)."""
+    if not (dist.is_initialized() and dist.get_world_size() > 1):
+        return p
+    t = torch.tensor([p["rows"], p["labels_above_gap_mismatch"], round(p["agree"] * p["rows"]),
+                      p["near_tie_rows"], 0 if p["counts_exact"] else 1], device=device,
+                     dtype=torch.float64)
+    dist.all_reduce(t)
+    rows = int(t[0].item())
+    return {"rows": rows, "labels_above_gap_mismatch": int(t[1].item()),
+            "agree": float(t[2].item()) / max(1, rows), "near_tie_rows": int(t[3].item()),
+            "counts_exact": int(t[4].item()) == 0}
+
+
+def time_reference_gpu(w: dict, steps: int, warmup: int, device) -> dict:
+    """The reference's own CUDA kernels (oracle/_ref, built from its sources) on the whole
+    workload on one GPU: a step is one iteration of the reference's loop (c_sq,
+    fkc::euclid_assign, torch.sort + sorted/indexed accumulate, finalize)."""
     from oracle import ref_lloyd
 
     if not ref_lloyd.available():
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "oracle/_ref not built (oracle/build_ref.sh needs the reference sources)"}))
-        return
+        return {"unavailable": "oracle/_ref not built (oracle/build_ref.sh needs the reference "
+                               "sources)"}
     ref = ref_lloyd.Reference()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    x, init = make_data(w, dev, seed=0)
+    x, init = make_data(w, device, seed=0)
     K = w["K"]
     x_sq = (x.float() ** 2).sum(-1).contiguous()
     cur = [init.clone()]
@@ -250,49 +322,73 @@ def run_reference_gpu(args, w: dict) -> None:
         sums, counts = ref.update(x, ids, K)
         cur[0] = ref.finalize(sums, counts, c)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
+    with ClockSampler(device.index) as clk:
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record()
-        torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+        torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
     c = cur[0]
     c_sq = (c.float() ** 2).sum(dim=-1).contiguous()
-    reps = 5
+    reps = 3
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ref.assign(x, c, x_sq=x_sq, c_sq=c_sq)
     a0.record()
     for _ in range(reps):
         ref.assign(x, c, x_sq=x_sq, c_sq=c_sq)
     a1.record()
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(device)
     t_assign = a0.elapsed_time(a1) / reps
     flops = 2.0 * w["B"] * w["N"] * K * w["D"]
     peaks = measured_peaks()
     tf = flops / (t_assign * 1e-3) / 1e12
-    peak, _ = tensor_peak(peaks, t_assign)
+    peak, peak_src = tensor_peak(peaks, t_assign)
+    del x, init, x_sq, cur
+    torch.cuda.empty_cache()
+    return {"ms_per_iter": ms, "assign_ms": t_assign, "assign_tflops": tf,
+            "assign_frac": tf / peak, "peak_src": peak_src, "steps": steps, "warmup": warmup,
+            "kernel": "reference assign_sm80_kernel (mma.sync, fp16 accumulation), built from "
+                      "its sources for sm_100",
+            "clocks": clk.summary()}
+
+
+def run_reference_gpu(args, w: dict) -> None:
+    """``--ref-device cuda``: the reference's own CUDA kernels as the line's value."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = time_reference_gpu(w, args.steps, args.warmup, dev)
+    if "unavailable" in r:
+        print(json.dumps({"impl": "reference", "unavailable": r["unavailable"]}))
+        return
+    ms = r["ms_per_iter"]
     print(json.dumps({
         "metric": "K-Means ms/iter", "value": ms, "unit": "ms/iter", "impl": "reference",
         "device": "cuda", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
         "dtype": DT_SHORT[w["dtype"]], "data": "synthetic",
-        "config": {"workload": args.workload, "B": w["B"], "N": w["N"], "K": K, "D": w["D"],
-                   "parallelism": "dp1"},
-        "assign_ms": t_assign, "assign_tflops": tf,
-        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak,
-                     "unit": "TFLOP/s", "frac": tf / peak,
-                     "kernel": "reference assign_sm80_kernel (mma.sync, fp16 accumulation)"},
-        "clocks": clk.summary(),
+        "config": {"workload": args.workload, "B": w["B"], "N": w["N"], "K": w["K"],
+                   "D": w["D"], "parallelism": "dp1"},
+        "assign_ms": r["assign_ms"], "assign_tflops": r["assign_tflops"],
+        "roofline": {"bound": "tensor", "achieved": r["assign_tflops"],
+                     "peak": r["assign_tflops"] / r["assign_frac"], "unit": "TFLOP/s",
+                     "frac": r["assign_frac"], "kernel": r["kernel"]},
+        "clocks": r["clocks"],
     }), flush=True)
 
 
 def run_reference_arm(args, w: dict) -> None:
-    """CPU port of the reference loop timed on the host cores (rank 0 only)."""
+    """The reference's loop on the host cores (rank 0 only): the CPU port of its Lloyd
+    iteration (the reference has no CPU path of its own) on a bounded sample of the
+    workload's own data distribution, plus, as ``reference_gpu``, the reference's own
+    CUDA kernels (built from its sources) on the whole workload on GPU 0."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -305,9 +401,9 @@ def run_reference_arm(args, w: dict) -> None:
     target = min(1.0, 120.0 / max(1, args.steps + args.warmup))
     n_s, _ = cpu_sample_rows(w, target_s=target)
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn((1, n_s, w["D"]), generator=g)
-    init = x[:, torch.randperm(n_s, generator=g)[:w["K"]]].contiguous()
+    # one batch element's worth of points drawn from the workload's distribution
+    w1 = dict(w, B=1)
+    x, init = make_data(w1, torch.device("cpu"), seed=0, n_rows=n_s, dtype=torch.float32)
     for _ in range(args.warmup):
         lloyd_cpu(x, init, 1)
     t0 = time.perf_counter()
@@ -317,6 +413,16 @@ def run_reference_arm(args, w: dict) -> None:
     scale = (w["B"] * w["N"]) / n_s
     ms = 1e3 * dt / args.steps * scale
     cores = torch.get_num_threads()
+    del x, init
+    ref_gpu = None
+    if torch.cuda.is_available() and not args.no_ref_gpu:
+        try:
+            dev = torch.device("cuda", 0)
+            torch.cuda.set_device(dev)
+            long = w["N"] * w["B"] * w["K"] > (1 << 33)  # c5: about a second per iteration
+            ref_gpu = time_reference_gpu(w, 2 if long else 5, 1, dev)
+        except Exception as e:  # the CPU line stands on its own
+            ref_gpu = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     line = {
         "metric": "K-Means ms/iter", "value": ms, "unit": "ms/iter", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -326,11 +432,15 @@ def run_reference_arm(args, w: dict) -> None:
                    "D": w["D"], "parallelism": "cpu"},
         "cpu_baseline": {"value": ms, "unit": "ms/iter", "cores": cores, "kind": "port",
                          "sample": (f"each step: 1 iteration on {n_s} of {w['B'] * w['N']} "
-                                    f"points (full K, D), fp32 CPU PyTorch Lloyd loop "
+                                    f"points drawn from the {args.workload} distribution "
+                                    f"({w['data']}" + (f", Zipf({w['zipf']})" if w["zipf"] else "")
+                                    + f"; full K, D), fp32 CPU PyTorch Lloyd loop "
                                     f"(oracle/cpu_lloyd.py; the reference has no CPU path), "
                                     f"scaled by {scale:.1f}x")},
+        "cpu_baseline_c1": cpu_baseline_c1(),
         "e2e": {"value": ms, "unit": "ms/iter", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "reference_gpu": ref_gpu,
     }
     print(json.dumps(line), flush=True)
 
@@ -409,6 +519,62 @@ def run_ours(args, w: dict) -> None:
         barrier_sync(dev)
     launches = int(_lib.lib.fkc_kernel_launches() - launches0)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, dev)
+    parity = None
+    if mm is None and not args.no_parity:
+        # the labels and counts of the last timed step, made against its input centroids
+        parity = sample_parity(x, bufs[(args.warmup + args.steps - 1) % 2], st.ids, st.counts)
+
+    # Per-rank split of the multi-GPU step (5 reps after the timed loop): local assign +
+    # update, the sums/counts reduction (+ finalize for the multicast path), barriers.
+    per_rank = None
+    if world > 1:
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        acc = torch.zeros(4, dtype=torch.float64)
+        for r in range(6):
+            barrier_sync(dev)
+            i = args.warmup + args.steps + r
+            a, b = bufs[i % 2], bufs[(i + 1) % 2]
+            evs[0].record(stream)
+            st.local(a)
+            evs[1].record(stream)
+            if mm is not None:
+                mm._barrier()
+                evs[2].record(stream)
+                mm.reduce_finalize(i, False)
+                evs[3].record(stream)
+                mm._barrier()
+            elif w["shard"] == "N":
+                evs[2].record(stream)
+                allreduce_sums_counts(st.sums, st.counts)
+                evs[3].record(stream)
+                st.finalize(a, b, False)
+            else:
+                evs[2].record(stream)
+                evs[3].record(stream)
+                st.finalize(a, b, False)
+            evs[4].record(stream)
+            torch.cuda.synchronize(dev)
+            if r == 0:
+                continue
+            acc += torch.tensor([evs[0].elapsed_time(evs[1]), evs[1].elapsed_time(evs[2]),
+                                 evs[2].elapsed_time(evs[3]), evs[3].elapsed_time(evs[4])],
+                                dtype=torch.float64) / 5
+        mine = acc.to(dev)
+        alls = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(alls, mine)
+        rows = [t.tolist() for t in alls]
+        if mm is not None:
+            per_rank = {"local_ms": [r_[0] for r_ in rows],
+                        "barrier_ms": [r_[1] + r_[3] for r_ in rows],
+                        "reduce_finalize_ms": [r_[2] for r_ in rows],
+                        "path": "multicast finalize (fkc_lloyd_finalize_multimem) between two "
+                                "symmetric-memory barriers"}
+        else:
+            per_rank = {"local_ms": [r_[0] for r_ in rows],
+                        "allreduce_ms": [r_[2] for r_ in rows],
+                        "finalize_ms": [r_[3] for r_ in rows],
+                        "path": "NCCL all-reduce of sums and counts + replicated finalize"
+                                if w["shard"] == "N" else "B-sharded, no collective"}
     if mm is not None:
         mm.release()  # every rank past the last multicast kernel before phase timings
 
@@ -449,6 +615,15 @@ def run_ours(args, w: dict) -> None:
         t_update += ev[1].elapsed_time(ev[2]) / reps
         t_fin += ev[2].elapsed_time(ev[3]) / reps
         t_iter += ev[3].elapsed_time(ev[4]) / reps
+    if mm is not None and not args.no_parity:
+        # the phase reps updated the multicast centroids in place: label them once more
+        _lib.check(_lib.lib.fkc_lloyd_assign(x.data_ptr(), cur_c.data_ptr(), st.ids.data_ptr(),
+                                             st.counts.data_ptr(), *dims, stream.cuda_stream),
+                   "assign")
+        torch.cuda.synchronize(dev)
+        parity = sample_parity(x, cur_c, st.ids, st.counts)
+    if parity is not None:
+        parity = reduce_parity(parity, dev)
     t_assign = max_over_ranks(t_assign, dev)
     t_update = max_over_ranks(t_update, dev)
     t_fin = max_over_ranks(t_fin, dev)
@@ -498,12 +673,43 @@ def run_ours(args, w: dict) -> None:
                "note": (f"one batch_kmeans_Euclid call of {iters} iterations per "
                         f"{iters} steps: pinned-host x + init copied in, labels + "
                         f"centroids copied out, inside the timed region")}
+        del x_host, init_host
+
+    # The reference's own end-to-end definition (benchmarks/bench_vs_triton.py:52-67):
+    # whole batch_kmeans_Euclid calls on device-resident x (set-up per call included),
+    # total time / iterations.
+    e2e_device = None
+    if not args.no_e2e:
+        iters = w["iters"]
+
+        def dev_call():
+            if world == 1:
+                return fkc.batch_kmeans_Euclid(x, K, max_iters=iters, tol=0.0,
+                                               init_centroids=init)
+            return batch_kmeans_Euclid_sharded(x, K, max_iters=iters, tol=0.0,
+                                               init_centroids=init, shard=w["shard"])
+
+        dev_call()
+        barrier_sync(dev)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps_dev = 3
+        g0.record(stream)
+        for _ in range(reps_dev):
+            dev_call()
+        g1.record(stream)
+        barrier_sync(dev)
+        e2e_device = {"value": max_over_ranks(g0.elapsed_time(g1) / (reps_dev * iters), dev),
+                      "unit": "ms/iter", "calls": reps_dev, "iters_per_call": iters,
+                      "note": "whole batch_kmeans_Euclid calls on device-resident x (workspace, "
+                              "norm rows and graph launch per call), as the reference's "
+                              "bench_vs_triton.py times them"}
 
     if rank == 0:
-        cpu = None
+        cpu = cpu_c1 = None
         if world == 1 and not args.no_cpu_baseline:
             try:
                 cpu = cpu_baseline(w, args.workload)
+                cpu_c1 = cpu_baseline_c1()
             except Exception as e:  # pragma: no cover
                 cpu = {"value": None, "error": str(e)}
         line = {
@@ -540,7 +746,11 @@ def run_ours(args, w: dict) -> None:
                                   "the timed step runs this rank's update, then reduces sums and "
                                   "counts across ranks inside the finalize")},
             "e2e": e2e,
+            "e2e_device": e2e_device,
+            "parity": parity,
+            "per_rank": per_rank,
             "cpu_baseline": cpu,
+            "cpu_baseline_c1": cpu_c1,
             "clocks": clk.summary(),
             "gpu_launches": launches,
         }
@@ -560,6 +770,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the float64 label check of the last timed step")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="reference arm: skip the reference_gpu timing of its CUDA kernels")
     ap.add_argument("--ref-device", default="cpu", choices=["cpu", "cuda"],
                     help="reference arm: the CPU port of its loop (default) or its own CUDA "
                          "kernels built from source under oracle/_ref")

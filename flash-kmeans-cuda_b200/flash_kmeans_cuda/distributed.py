@@ -195,15 +195,13 @@ class MultimemLloyd:
         self.centroids.copy_(c)
         self.state.set_centroids(self.centroids)
 
-    def step(self, it: int, want_shift: bool) -> Optional[torch.Tensor]:
-        """One iteration in place on ``self.centroids``; returns the (1,) shift
-        tensor when ``want_shift`` (valid once the stream reaches it)."""
+    def reduce_finalize(self, it: int, want_shift: bool) -> None:
+        """This rank's slice of the centroid rows: the ranks' sums and counts summed
+        through the NVSwitch, new rows written to every rank (between two barriers)."""
         from ._lib import check, lib
 
         p = it & 1
         st = self.state
-        st.local(self.centroids)
-        self._barrier()
         B, K, D, code = self.dims
         with torch.cuda.device(st.device):
             check(lib.fkc_lloyd_finalize_multimem(
@@ -212,7 +210,15 @@ class MultimemLloyd:
                 self.shift[1 - p:2 - p].data_ptr() if want_shift else None,
                 self.rows[0], self.rows[1], B, K, D, code, st._stream()),
                 "fkc_lloyd_finalize_multimem")
+
+    def step(self, it: int, want_shift: bool) -> Optional[torch.Tensor]:
+        """One iteration in place on ``self.centroids``; returns the (1,) shift
+        tensor when ``want_shift`` (valid once the stream reaches it)."""
+        self.state.local(self.centroids)
         self._barrier()
+        self.reduce_finalize(it, want_shift)
+        self._barrier()
+        p = it & 1
         return self.shift[p:p + 1] if want_shift else None
 
 
