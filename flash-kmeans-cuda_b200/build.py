@@ -29,6 +29,7 @@ BUILD_DIR = PKG_ROOT / "_build"
 INCLUDE = REPO_ROOT / "include"
 
 CORE_SOURCES = ["capi.cu", "assign_tc.cu", "norm_ext.cu", "assign_simt.cu", "update.cu",
+                "update_det.cu",
                 "finalize.cu", "lloyd_graph.cu", "assign_noalloc.cu", "selftest.cu"]
 CORE_LIB = OUT_DIR / "libfkc_b200.so"
 TORCH_API_LIB = OUT_DIR / "libflash_kmeans_cuda.so"

@@ -204,6 +204,7 @@ struct LloydWs {
   uint8_t* splitk = nullptr;  // assign_splitk_bytes(), tensor-core path
   uint8_t* x3 = nullptr;      // (B,N,3D) bf16, split-fp32 tensor-core path
   uint8_t* c3 = nullptr;      // (B,K,3D) bf16, split-fp32 tensor-core path
+  DetWorkspace det{};         // deterministic update (update_det.cu)
 };
 
 constexpr size_t kCtlBytes = 256;
@@ -211,7 +212,8 @@ constexpr size_t kCtlBytes = 256;
 size_t lloyd_ws_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   return assign_ws_bytes(B, N, K, D, dtype) + align_up(static_cast<size_t>(B * K) * 4, 256) +
          update_workspace_bytes(B, N, K) + update_plan_bytes(B, N, K, D) + kCtlBytes +
-         (tc_shape_ok(D, dtype) ? assign_splitk_bytes() : 0);
+         (tc_shape_ok(D, dtype) ? assign_splitk_bytes() : 0) +
+         det_update_bytes(B, N, K, D, dtype);
 }
 
 int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
@@ -250,6 +252,8 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
   out->upd = carve_update_workspace(p, B, N, K);
   p += update_workspace_bytes(B, N, K);
   out->plan = carve_update_plan(p, B, N, K, D);
+  p += update_plan_bytes(B, N, K, D);
+  out->det = carve_det(p, B, N, K, D, dtype);
   return FKC_OK;
 }
 
@@ -481,6 +485,9 @@ FKC_CAPI_EXPORT int fkc_lloyd_update(const void* x, const int32_t* ids, const in
   FKC_REQUIRE(x && ids && counts && sums, "null argument");
   LloydWs w;
   FKC_TRY(carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w));
+  if (det_update_ok(w.det, x, sums, nullptr, nullptr, N, K, D, dtype))
+    return launch_det_update(x, ids, counts, w.upd, w.det, sums, nullptr, nullptr, nullptr,
+                             nullptr, nullptr, B, N, K, D, dtype, as_stream(stream));
   return update_from_ids(x, ids, sums, const_cast<int32_t*>(counts), true, w.upd, B, N, K, D,
                          dtype, as_stream(stream));
 }
@@ -513,6 +520,20 @@ FKC_CAPI_EXPORT int fkc_lloyd_iter(const void* x, const void* old_c, void* new_c
                                    float* sums, int32_t* counts, float* shift_out, int64_t B,
                                    int64_t N, int64_t K, int64_t D, int dtype, void* workspace,
                                    size_t workspace_bytes, fkc_stream_t stream) {
+  {
+    // Deterministic path: assign -> stable counting sort -> span gather -> join +
+    // finalize (every float addition in an order fixed by the labels).
+    LloydWs w;
+    if (old_c != nullptr && new_c != nullptr &&
+        carve_lloyd(workspace, workspace_bytes, B, N, K, D, dtype, &w) == FKC_OK &&
+        det_update_ok(w.det, x, sums, old_c, new_c, N, K, D, dtype)) {
+      FKC_TRY(fkc_lloyd_assign(x, old_c, ids, counts, B, N, K, D, dtype, workspace,
+                               workspace_bytes, stream));
+      return launch_det_update(x, ids, counts, w.upd, w.det, sums, old_c, new_c, w.c_sq, w.cext,
+                               shift_out, B, N, K, D, dtype, as_stream(stream));
+    }
+    clear_error();
+  }
   if (x != nullptr && old_c != nullptr && new_c != nullptr && sums != nullptr &&
       N <= 32 * K && fused_update_ok(x, old_c, new_c, sums, D, dtype)) {
     // Single GPU, small clusters (at most 32 rows on average): the update and
