@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(256) det_fixup_kernel(
     const float* __restrict__ part, const int32_t* __restrict__ counts,
     const int32_t* __restrict__ offsets, float* __restrict__ sums, const T* old_c, T* new_c,
     float* __restrict__ c_sq_out, uint8_t* __restrict__ cext_out, float* __restrict__ shift_out,
-    int K, int Pc, int ncta_per_batch, int64_t BK) {
+    int N, int K, int Pc, int ncta_per_batch, int64_t BK) {
   constexpr int kVec = 16 / sizeof(T);
   constexpr int G = 32 / L;
   constexpr int D = L * kVec;
@@ -469,8 +469,10 @@ __global__ void __launch_bounds__(256) det_fixup_kernel(
     float* srow = sums + kg * D + i * kVec;
     bool write = true;
     if (cnt > 0) {
-      const int cs = offsets[kg];
-      const int ca = cs / Pc, cb = (cs + cnt - 1) / Pc;
+      // (counts consistent with the labels keep cs + cnt <= N; clamped so that a
+      // caller's inconsistent counts can never index past the partial slots)
+      const int cs = min(max(offsets[kg], 0), N - 1);
+      const int ca = cs / Pc, cb = (min(cs + cnt, N) - 1) / Pc;
       if (ca == cb) {
         write = false;  // whole cluster inside one CTA span: the gather stored it
         if (!FINAL) continue;
@@ -635,14 +637,14 @@ int launch_det_typed(const void* x, const int32_t* counts, const UpdateWorkspace
                       0, stream, static_cast<const float*>(dw.part), counts,
                       static_cast<const int32_t*>(uw.offsets), sums, static_cast<const T*>(old_c),
                       static_cast<T*>(new_c), c_sq, static_cast<uint8_t*>(cext), shift,
-                      static_cast<int>(K), pc, static_cast<int>(ncta), BK);
+                      static_cast<int>(N), static_cast<int>(K), pc, static_cast<int>(ncta), BK);
   }
   return launch_pdl(det_fixup_kernel<T, L, false>, dim3(static_cast<unsigned>(blocks)), dim3(256),
                     0, stream, static_cast<const float*>(dw.part), counts,
                     static_cast<const int32_t*>(uw.offsets), sums, static_cast<const T*>(nullptr),
                     static_cast<T*>(nullptr), static_cast<float*>(nullptr),
                     static_cast<uint8_t*>(nullptr), static_cast<float*>(nullptr),
-                    static_cast<int>(K), pc, static_cast<int>(ncta), BK);
+                    static_cast<int>(N), static_cast<int>(K), pc, static_cast<int>(ncta), BK);
 }
 
 template <typename T>

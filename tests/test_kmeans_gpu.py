@@ -275,7 +275,7 @@ def test_graph_loop_matches_stepwise(cuda_device, dtype, tol):
     ("float16", 1, 524288, 8192, 128, 1.1),   # c3 shape: the bench workload
     ("bfloat16", 32, 16384, 1024, 64, 0.0),   # c4 shape
     ("float32", 2, 50000, 3000, 32, 1.1),
-    ("float16", 1, 200000, 40000, 64, 0.0),   # K > 16384: two-warp sort chunks
+    ("float16", 1, 200000, 40000, 64, 0.0),   # K > 32768: one counter row per sort chunk
 ])
 def test_update_is_deterministic(cuda_device, dtype, B, N, K, D, zipf):
     """Two runs of the same Lloyd step give bit-identical sums, counts and
