@@ -87,7 +87,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilog
 constexpr int kEpiWarpBegin = 2;
 constexpr int kParts = kEpiWarps / 4;          // column slices of an item
 constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
-constexpr int kMaxTcD = 384;  // D > 256 runs on CTA pairs (each CTA holds half a chunk)
+constexpr int kMaxTcD = 512;  // D > 256 runs on CTA pairs (each CTA holds half a chunk)
 // Split mode partials: 2 slots per CTA x rows of a tile x (f32 score, i32 index).
 constexpr int kSplitMaxCtas = 256;
 constexpr int kSplitMaxRows = 256;
@@ -143,7 +143,8 @@ struct Cfg {
   static_assert(kSmemBytes == layout_bytes(kXS), "layout size");
   static_assert(NC % 32 == 0 && NC >= 32 && NC <= 256, "UMMA N");
   static_assert(kNB % 16 == 0, "TMA box rows / UMMA N granularity");
-  static_assert(NC == 128 || NC == 256, "accumulator slots tile the 512 TMEM columns");
+  static_assert(NC == 64 || NC == 128 || NC == 256, "accumulator slots tile the 512 TMEM columns");
+  static_assert(NC >= 128 || CG == 2, "64-centroid chunks only on CTA pairs (UMMA M = 256)");
   static_assert(kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
 
@@ -385,7 +386,7 @@ struct SegIter {
   }
 };
 
-template <int DB, int MT, int NC, int ST, bool BF16, int CG>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     assign_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_aext,
@@ -589,21 +590,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             // epilogue work of this sub-partition alone).
             const uint32_t a_lo = umma_desc_lo(sb + C::kOffX + xi * C::kXSubBytes);
             const uint32_t b_lo = umma_desc_lo(c_stage);
+            // SPLIT (fp32 inputs): rows hold [hi | lo] bf16 halves of PB blocks
+            // each; the three passes accumulate hi.hi, hi.lo and lo.hi into the
+            // same accumulator (A's lo half in pass 2, B's lo half in pass 1).
+            constexpr int kPasses = SPLIT ? 3 : 1;
+            constexpr int PB = SPLIT ? DB / 2 : DB;  // 64-element blocks per pass
+            static_assert(!SPLIT || DB % 2 == 0, "split rows: two halves of whole blocks");
 #pragma unroll
-            for (int ks = 0; ks < DB * 4; ++ks) {
-              if (ks < ksteps) {
-                // K step of 16 elements = 32 bytes = 2 start units; a 64-element
-                // swizzle block is block_bytes / 16 units further.
-                constexpr uint32_t kStepA = (kRowsPerSub * kKBlockBytes) >> 4;
-                constexpr uint32_t kStepB = C::kCBlockBytes >> 4;
-                const uint32_t da = (ks >> 2) * kStepA + (ks & 3) * 2;
-                const uint32_t db = (ks >> 2) * kStepB + (ks & 3) * 2;
-                // Opaque to the compiler: the first step's "overwrite" flag stays
-                // a runtime predicate.
-                uint32_t accf = ks > 0 ? 1u : 0u;
-                asm volatile("" : "+r"(accf));
-                mma<CG>(d_tmem, umma_desc(a_lo + da, kHi128), umma_desc(b_lo + db, kHi128),
-                        idesc, accf);
+            for (int pass = 0; pass < kPasses; ++pass) {
+              const int ao = (SPLIT && pass == 2) ? PB : 0;
+              const int bo = (SPLIT && pass == 1) ? PB : 0;
+#pragma unroll
+              for (int ks = 0; ks < PB * 4; ++ks) {
+                if (ks < ksteps) {
+                  // K step of 16 elements = 32 bytes = 2 start units; a 64-element
+                  // swizzle block is block_bytes / 16 units further.
+                  constexpr uint32_t kStepA = (kRowsPerSub * kKBlockBytes) >> 4;
+                  constexpr uint32_t kStepB = C::kCBlockBytes >> 4;
+                  const uint32_t da = ((ks >> 2) + ao) * kStepA + (ks & 3) * 2;
+                  const uint32_t db = ((ks >> 2) + bo) * kStepB + (ks & 3) * 2;
+                  // Opaque to the compiler: the first step's "overwrite" flag stays
+                  // a runtime predicate.
+                  uint32_t accf = (pass > 0 || ks > 0) ? 1u : 0u;
+                  asm volatile("" : "+r"(accf));
+                  mma<CG>(d_tmem, umma_desc(a_lo + da, kHi128), umma_desc(b_lo + db, kHi128),
+                          idesc, accf);
+                }
               }
             }
             mma<CG>(d_tmem, umma_desc(umma_desc_lo(sb + C::kOffAext + xi * C::kAextSubBytes), kHi32),
@@ -938,12 +950,14 @@ int cta_group_choice() {
   return v;
 }
 
-template <int DB, int MT, int NC, int ST, bool BF16, int CG>
+// D: elements per stored row (split fp32: 2 * Dp, the [hi | lo] halves);
+// ksteps: K steps of 16 elements per pass (D / 16, or the fp32 row's D / 16).
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT>
 int launch_tc_impl(const void* x, const void* centroids, const void* aext, const void* cext,
                    int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
-                   int64_t K, int64_t D, cudaStream_t stream) {
+                   int64_t K, int64_t D, int ksteps, cudaStream_t stream) {
   using C = Cfg<DB, MT, NC, ST, CG>;
-  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG>;
+  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG, SPLIT>;
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   FKC_CUDA_TRY(
@@ -1021,8 +1035,8 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
   }
   cfg.gridDim = dim3(static_cast<unsigned>(CG * n_units), 1, 1);
   FKC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tm_x, tm_aext, tm_c, tm_cext, ids, counts,
-                                  static_cast<int>(N), static_cast<int>(K),
-                                  static_cast<int>(D / 16), static_cast<int>(tiles_per_batch),
+                                  static_cast<int>(N), static_cast<int>(K), ksteps,
+                                  static_cast<int>(tiles_per_batch),
                                   static_cast<int>(total_tiles), pval, pidx,
                                   device_error_word()));
   count_launches(1);
@@ -1040,12 +1054,33 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
 template <bool BF16, int CG>
 int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, const void* cext,
                        int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
-                       int64_t K, int64_t D, cudaStream_t stream) {
+                       int64_t K, int64_t D, int split_d, cudaStream_t stream) {
   // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
 #define FKC_TC(DB_, MT_, NC_, ST_, CG_)                                                    \
-  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_>(x, centroids, aext, cext, ids, counts,     \
-                                                (CG_) == 1 ? splitk_ws : nullptr, B, N, K, \
-                                                D, stream)
+  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_, false>(                                    \
+      x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
+      static_cast<int>(D / 16), stream)
+#define FKC_TC_SPLIT(DB_, MT_, NC_, ST_, CG_)                                              \
+  launch_tc_impl<DB_, MT_, NC_, ST_, true, CG_, true>(                                     \
+      x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
+      split_d / 16, stream)
+  if constexpr (BF16 && CG == 1) {
+    if (split_d > 0) {
+      // fp32 rows as [hi | lo] bf16 halves of Dp = D / 2 elements (a multiple of
+      // 64): the configurations of a bf16 row of D = 2 Dp elements, each item
+      // running three passes of split_d / 16 K steps.
+      if (D <= 128) return FKC_TC_SPLIT(2, 2, 256, 2, 1);
+      if (D <= 256) return FKC_TC_SPLIT(4, 1, 128, 2, 1);
+      if (D <= 384) return FKC_TC_SPLIT(6, 1, 128, 2, 2);
+      return FKC_TC_SPLIT(8, 1, 64, 2, 2);
+    }
+  }
+  if (D > 384) {
+    // 384 < D <= 512: CTA pairs with 64-centroid chunks, each CTA holding 32
+    // centroid rows per stage (x 128 KB + 2 x 32 KB per CTA); an item is
+    // M = 256 x N = 64 x K = D, long enough that the MMA stream dominates.
+    return FKC_TC(8, 1, 64, 2, 2);
+  }
   if (D > 256) {
     // A single CTA cannot hold a 128-row x sub-tile plus two stages of a
     // 128-centroid chunk in 227 KB. A CTA pair splits every chunk: each CTA
@@ -1066,6 +1101,7 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
     return FKC_TC(4, 1, 128, 2, 1);
   }
 #undef FKC_TC
+#undef FKC_TC_SPLIT
 }
 
 }  // namespace
@@ -1082,20 +1118,26 @@ bool assign_tc_supported(int64_t D, int dtype) {
 
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
                      int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
-                     int64_t K, int64_t D, int dtype, cudaStream_t stream) {
+                     int64_t K, int64_t D, int dtype, cudaStream_t stream, int split_d) {
   FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
               static_cast<long long>(D), dtype);
+  FKC_REQUIRE(split_d == 0 || (dtype == FKC_DTYPE_BF16 && D % 128 == 0 && split_d % 16 == 0 &&
+                               split_d > 0 && split_d <= D / 2),
+              "assign_tc: bad split rows (D=%lld, split_d=%d)", static_cast<long long>(D),
+              split_d);
   const bool bf16 = dtype == FKC_DTYPE_BF16;
-  const bool pairs = cta_group_choice() == 2;
+  // Split fp32 rows always run on single CTAs up to D = 256 (the pair choice
+  // applies to 16-bit inputs).
+  const bool pairs = cta_group_choice() == 2 && split_d == 0;
   if (bf16)
     return pairs ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws,
-                                               B, N, K, D, stream)
+                                               B, N, K, D, 0, stream)
                  : launch_tc_dispatch<true, 1>(x, centroids, aext, cext, ids, counts, splitk_ws,
-                                               B, N, K, D, stream);
+                                               B, N, K, D, split_d, stream);
   return pairs ? launch_tc_dispatch<false, 2>(x, centroids, aext, cext, ids, counts, splitk_ws, B,
-                                              N, K, D, stream)
+                                              N, K, D, 0, stream)
                : launch_tc_dispatch<false, 1>(x, centroids, aext, cext, ids, counts, splitk_ws, B,
-                                              N, K, D, stream);
+                                              N, K, D, 0, stream);
 }
 
 }  // namespace fkc

@@ -136,16 +136,17 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 namespace {
 
 // fp32 inputs on the tensor cores: x and the centroids are split into bf16
-// hi/lo rows of 3D elements (hi.hi + hi.lo + lo.hi, see launch_split_bf16), so
-// 3D must fit the bf16 kernel (D <= 128).
+// [hi | lo] rows of 2 Dp elements (Dp = D rounded up to 64; the kernel runs the
+// hi.hi, hi.lo and lo.hi passes, see launch_split_bf16), so 2 Dp must fit the
+// bf16 kernel (D <= 256).
 bool split_f32(int64_t D, int dtype) {
-  return dtype == FKC_DTYPE_F32 && D >= 16 && D <= 128 && D % 16 == 0;
+  return dtype == FKC_DTYPE_F32 && D >= 16 && D <= 256 && D % 16 == 0;
 }
 
 // Shape/dtype eligibility of the tensor-core assignment, independent of the
 // device (workspace sizes must not depend on which GPU is current).
 bool tc_shape_ok(int64_t D, int dtype) {
-  return ((dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 384 &&
+  return ((dtype == FKC_DTYPE_F16 || dtype == FKC_DTYPE_BF16) && D >= 16 && D <= 512 &&
           D % 16 == 0) ||
          split_f32(D, dtype);
 }
@@ -155,7 +156,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool use_tc(const void* x, const void* c, int64_t D, int dtype) {
   const bool split = split_f32(D, dtype);
   return tc_shape_ok(D, dtype) && !force_safe_path() && aligned16(x) && aligned16(c) &&
-         assign_tc_supported(split ? 3 * D : D, split ? FKC_DTYPE_BF16 : dtype);
+         assign_tc_supported(split ? split_row_elems(D) : D, split ? FKC_DTYPE_BF16 : dtype);
 }
 
 }  // namespace
@@ -166,11 +167,12 @@ bool assign_may_use_tc_host(const void* x, const void* c, int64_t D, int dtype) 
 
 namespace {
 
-// Operand rows of the split-fp32 path: x3 (B, N, 3D) and c3 (B, K, 3D) bf16.
+// Operand rows of the split-fp32 path: x2 (B, N, 2 Dp) and c2 (B, K, 2 Dp) bf16.
 size_t split_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   if (!split_f32(D, dtype)) return 0;
-  return align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256) +
-         align_up(static_cast<size_t>(B * K * 3 * D) * 2, 256);
+  const int64_t E = split_row_elems(D);
+  return align_up(static_cast<size_t>(B * N * E) * 2, 256) +
+         align_up(static_cast<size_t>(B * K * E) * 2, 256);
 }
 
 int check_dims(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
@@ -202,8 +204,8 @@ struct LloydWs {
   UpdatePlan plan{};          // fused update + finalize (single-GPU iteration)
   LoopCtl* ctl = nullptr;     // whole-loop graph control block
   uint8_t* splitk = nullptr;  // assign_splitk_bytes(), tensor-core path
-  uint8_t* x3 = nullptr;      // (B,N,3D) bf16, split-fp32 tensor-core path
-  uint8_t* c3 = nullptr;      // (B,K,3D) bf16, split-fp32 tensor-core path
+  uint8_t* x3 = nullptr;      // (B,N,2Dp) bf16 [hi|lo], split-fp32 tensor-core path
+  uint8_t* c3 = nullptr;      // (B,K,2Dp) bf16 [hi|lo], split-fp32 tensor-core path
   DetWorkspace det{};         // deterministic update (update_det.cu)
 };
 
@@ -243,10 +245,11 @@ int carve_lloyd(void* ws, size_t ws_bytes, int64_t B, int64_t N, int64_t K, int6
     out->aext = p;
     p += align_up(static_cast<size_t>(B * N) * 32, 256);
     if (split_f32(D, dtype)) {
+      const int64_t E = split_row_elems(D);
       out->x3 = p;
-      p += align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256);
+      p += align_up(static_cast<size_t>(B * N * E) * 2, 256);
       out->c3 = p;
-      p += align_up(static_cast<size_t>(B * K * 3 * D) * 2, 256);
+      p += align_up(static_cast<size_t>(B * K * E) * 2, 256);
     }
   }
   out->upd = carve_update_workspace(p, B, N, K);
@@ -356,12 +359,13 @@ FKC_CAPI_EXPORT int fkc_assign(const void* x, const void* centroids, const float
     FKC_TRY(launch_xnorm_ext(x, aext, B, N, D, dtype, st));
     FKC_TRY(launch_cnorm_ext(centroids, c_sq, cext, nullptr, B, K, D, dtype, st));
     if (split) {
+      const int64_t E = split_row_elems(D);
       uint8_t* x3 = cext + align_up(static_cast<size_t>(B * K) * 32, 256);
-      uint8_t* c3 = x3 + align_up(static_cast<size_t>(B * N * 3 * D) * 2, 256);
-      FKC_TRY(launch_split_bf16(x, x3, B * N, D, true, st));
-      FKC_TRY(launch_split_bf16(centroids, c3, B * K, D, false, st));
-      return launch_assign_tc(x3, c3, aext, cext, ids, nullptr, nullptr, B, N, K, 3 * D,
-                              FKC_DTYPE_BF16, st);
+      uint8_t* c3 = x3 + align_up(static_cast<size_t>(B * N * E) * 2, 256);
+      FKC_TRY(launch_split_bf16(x, x3, B * N, D, st));
+      FKC_TRY(launch_split_bf16(centroids, c3, B * K, D, st));
+      return launch_assign_tc(x3, c3, aext, cext, ids, nullptr, nullptr, B, N, K, E,
+                              FKC_DTYPE_BF16, st, static_cast<int>(D));
     }
     return launch_assign_tc(x, centroids, aext, cext, ids, nullptr, nullptr, B, N, K, D, dtype,
                             st);
@@ -436,7 +440,7 @@ FKC_CAPI_EXPORT int fkc_lloyd_prepare(const void* x, int64_t B, int64_t N, int64
   // The fused update's per-cluster accumulators start (and stay) zero.
   FKC_TRY(launch_zero_fill(w.plan.done, w.plan.zero_bytes, as_stream(stream)));
   if (w.aext != nullptr) FKC_TRY(launch_xnorm_ext(x, w.aext, B, N, D, dtype, as_stream(stream)));
-  if (w.x3 != nullptr) FKC_TRY(launch_split_bf16(x, w.x3, B * N, D, true, as_stream(stream)));
+  if (w.x3 != nullptr) FKC_TRY(launch_split_bf16(x, w.x3, B * N, D, as_stream(stream)));
   return FKC_OK;
 }
 
@@ -465,9 +469,9 @@ FKC_CAPI_EXPORT int fkc_lloyd_assign(const void* x, const void* centroids, int32
   if (w.aext != nullptr && use_tc(x, centroids, D, dtype)) {
     if (w.x3 != nullptr) {
       // fp32: this iteration's centroids as split bf16 rows (x3: prepare).
-      FKC_TRY(launch_split_bf16(centroids, w.c3, B * K, D, false, st));
-      return launch_assign_tc(w.x3, w.c3, w.aext, w.cext, ids, counts, w.splitk, B, N, K, 3 * D,
-                              FKC_DTYPE_BF16, st);
+      FKC_TRY(launch_split_bf16(centroids, w.c3, B * K, D, st));
+      return launch_assign_tc(w.x3, w.c3, w.aext, w.cext, ids, counts, w.splitk, B, N, K,
+                              split_row_elems(D), FKC_DTYPE_BF16, st, static_cast<int>(D));
     }
     return launch_assign_tc(x, centroids, w.aext, w.cext, ids, counts, w.splitk, B, N, K, D,
                             dtype, st);

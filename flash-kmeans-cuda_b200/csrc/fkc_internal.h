@@ -88,18 +88,22 @@ int launch_xnorm_ext(const void* x, void* aext, int64_t B, int64_t N, int64_t D,
 // Centroid terms: extension rows cext[b,k,:] = {1,1,1,h1,h2,h3,0...} with
 // h = -0.5*c_sq (cext nullable) and/or c_sq_out[b,k] (nullable). c_sq is taken
 // from `c_sq` when non-null, otherwise computed from the centroids.
-// fp32 rows (rows x D) -> bf16 rows (rows x 3D) whose bf16 dot products give
-// fp32 dot products to ~2^-16: point side [hi|hi|lo], centroid side [hi|lo|hi].
-int launch_split_bf16(const void* src, void* dst, int64_t rows, int64_t D, bool point_side,
-                      cudaStream_t stream);
+// fp32 rows (rows x D) -> bf16 rows (rows x 2 Dp, Dp = D rounded up to 64):
+// [hi | 0 | lo | 0] with hi = bf16(v), lo = bf16(v - hi). The tensor-core
+// assignment accumulates hi.hi + hi.lo + lo.hi (three passes), the fp32 dot
+// product to ~2^-16 |x||c|.
+int64_t split_row_elems(int64_t D);  // 2 * Dp
+int launch_split_bf16(const void* src, void* dst, int64_t rows, int64_t D, cudaStream_t stream);
 int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float* c_sq_out,
                      int64_t B, int64_t K, int64_t D, int dtype, cudaStream_t stream);
 
 // splitk_ws (nullable, assign_splitk_bytes()): lets the kernel balance an
 // uneven last wave by sharing tiles between CTAs (merged by a fixup kernel).
+// split_d > 0: x and centroids are split fp32 rows (launch_split_bf16) of
+// D = split_row_elems(split_d) bf16 elements.
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
                      int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
-                     int64_t K, int64_t D, int dtype, cudaStream_t stream);
+                     int64_t K, int64_t D, int dtype, cudaStream_t stream, int split_d = 0);
 size_t assign_splitk_bytes();
 
 int launch_assign_simt(const void* x, const void* centroids, const float* x_sq,

@@ -72,39 +72,42 @@ __global__ void cnorm_ext_kernel(const T* __restrict__ c, const float* __restric
   }
 }
 
-// fp32 rows -> bf16 rows of 3D elements for the tensor-core assignment of fp32
-// inputs: point side [hi | hi | lo], centroid side [hi | lo | hi] with
-// hi = bf16(v), lo = bf16(v - hi), so the bf16 dot product of the two rows is
-// hi.hi + hi.lo + lo.hi = x.c up to about 2^-16 |x||c| (the lo.lo term and the
-// rounding of lo are dropped). One thread per 4 elements.
-template <bool POINT_SIDE>
+// fp32 rows -> split bf16 rows for the tensor-core assignment of fp32 inputs:
+// [hi | 0 | lo | 0], each half Dp = D rounded up to 64 elements, hi = bf16(v),
+// lo = bf16(v - hi) (round to nearest even). The assignment kernel accumulates
+// three passes, hi.hi + hi.lo + lo.hi, which is x.c up to about 2^-16 |x||c|
+// (the lo.lo term and the rounding of lo are dropped). Points and centroids use
+// the same layout. One thread per 4 elements of a half.
 __global__ void split_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
-                                  int64_t rows, int D) {
+                                  int64_t rows, int D, int Dp) {
   pdl_wait();
-  const int q = D / 4;  // float4 per row
+  const int q = Dp / 4;  // 4-element groups per half
   const int64_t total = rows * q;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
        t += stride) {
     const int64_t r = t / q;
     const int c = static_cast<int>(t - r * q) * 4;
-    const float4 v = *reinterpret_cast<const float4*>(src + r * D + c);
-    const float f[4] = {v.x, v.y, v.z, v.w};
-    uint32_t hi[2], lo[2];
+    uint2 H = make_uint2(0u, 0u), Lo = make_uint2(0u, 0u);
+    if (c < D) {
+      const float4 v = *reinterpret_cast<const float4*>(src + r * D + c);
+      const float f[4] = {v.x, v.y, v.z, v.w};
+      uint32_t hi[2], lo[2];
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * e]);
-      const __nv_bfloat16 h1 = __float2bfloat16_rn(f[2 * e + 1]);
-      const __nv_bfloat16 l0 = __float2bfloat16_rn(f[2 * e] - __bfloat162float(h0));
-      const __nv_bfloat16 l1 = __float2bfloat16_rn(f[2 * e + 1] - __bfloat162float(h1));
-      hi[e] = __bfloat16_as_ushort(h0) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-      lo[e] = __bfloat16_as_ushort(l0) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+      for (int e = 0; e < 2; ++e) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(f[2 * e]);
+        const __nv_bfloat16 h1 = __float2bfloat16_rn(f[2 * e + 1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(f[2 * e] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(f[2 * e + 1] - __bfloat162float(h1));
+        hi[e] = __bfloat16_as_ushort(h0) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+        lo[e] = __bfloat16_as_ushort(l0) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+      }
+      H = make_uint2(hi[0], hi[1]);
+      Lo = make_uint2(lo[0], lo[1]);
     }
-    const uint2 H = make_uint2(hi[0], hi[1]), Lo = make_uint2(lo[0], lo[1]);
-    __nv_bfloat16* row = dst + r * 3 * D + c;
+    __nv_bfloat16* row = dst + r * 2 * Dp + c;
     *reinterpret_cast<uint2*>(row) = H;
-    *reinterpret_cast<uint2*>(row + D) = POINT_SIDE ? H : Lo;
-    *reinterpret_cast<uint2*>(row + 2 * D) = POINT_SIDE ? Lo : H;
+    *reinterpret_cast<uint2*>(row + Dp) = Lo;
   }
 }
 
@@ -164,21 +167,19 @@ int launch_cnorm_ext(const void* centroids, const float* c_sq, void* cext, float
   }
 }
 
-int launch_split_bf16(const void* src, void* dst, int64_t rows, int64_t D, bool point_side,
-                      cudaStream_t stream) {
+int64_t split_row_elems(int64_t D) { return 2 * ((D + 63) / 64 * 64); }
+
+int launch_split_bf16(const void* src, void* dst, int64_t rows, int64_t D, cudaStream_t stream) {
   FKC_REQUIRE(D % 4 == 0, "split_bf16: D must be a multiple of 4");
-  const int64_t threads = rows * (D / 4);
+  const int64_t Dp = split_row_elems(D) / 2;
+  const int64_t threads = rows * (Dp / 4);
   int64_t blocks = (threads + 255) / 256;
   const int64_t cap = static_cast<int64_t>(sm_count_or_default_ne()) * 16;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  const dim3 grid(static_cast<unsigned>(blocks));
-  const float* s = static_cast<const float*>(src);
-  __nv_bfloat16* d = static_cast<__nv_bfloat16*>(dst);
-  return point_side ? launch_pdl(split_bf16_kernel<true>, grid, dim3(256), 0, stream, s, d, rows,
-                                 static_cast<int>(D))
-                    : launch_pdl(split_bf16_kernel<false>, grid, dim3(256), 0, stream, s, d, rows,
-                                 static_cast<int>(D));
+  return launch_pdl(split_bf16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                    static_cast<const float*>(src), static_cast<__nv_bfloat16*>(dst), rows,
+                    static_cast<int>(D), static_cast<int>(Dp));
 }
 
 }  // namespace fkc

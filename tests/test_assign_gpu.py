@@ -4,7 +4,7 @@ Bar (per config): labels identical wherever the top-2 distance gap exceeds
 1e-3 * ||x||^2, and >= 99.9% identical overall. Shapes cover the reference's
 edge cases (tests/test_shapes.py:14-20, tests/test_persistent.py:26-118,
 tests/test_mma_optin.py:35-42): tail tiles, K = 1, K around chunk widths,
-D = 64/96/128/192/256/320/384, B > 1.
+D = 16..512, B > 1.
 """
 
 from __future__ import annotations
@@ -61,6 +61,8 @@ SHAPES = [
     (1, 2048, 4096, 128),
     (1, 1500, 300, 320),    # D > 256: CTA-pair kernel, 64 centroid rows per CTA
     (2, 3000, 700, 384),
+    (1, 2000, 500, 448),    # D > 384: CTA pairs with 64-centroid chunks, 32 rows per CTA
+    (2, 1700, 333, 512),
 ]
 
 
@@ -132,6 +134,21 @@ def test_fp32_and_odd_d(cuda_device, B, N, K, D):
         c = subset_init(x, K, seed=2)
         ids = _assign_gpu(x, c)
         _check(ids, orc.assign(to_np(x), to_np(c)), f"{dtype} D={D}")
+
+
+@pytest.mark.parametrize("B,N,K,D", [(1, 3000, 500, 144), (2, 2000, 300, 192),
+                                     (1, 2500, 700, 256), (1, 1000, 100, 384)])
+def test_fp32_tensor_core_widths(cuda_device, B, N, K, D):
+    """fp32 up to D = 256 runs on the tensor cores as split bf16 rows ([hi | lo] halves,
+    three accumulating passes); D = 384 keeps the CUDA-core kernel. The assignment
+    workspace is non-zero exactly for the tensor-core route."""
+    from flash_kmeans_cuda import _lib
+
+    x = mixture(B, N, D, max(K // 4, 2), seed=N + D, dtype="float32")
+    c = subset_init(x, K, seed=4)
+    assert (_lib.lib.fkc_assign_workspace_size(B, N, K, D, 2) > 0) == (D <= 256)
+    ids = _assign_gpu(x, c)
+    _check(ids, orc.assign(to_np(x), to_np(c)), f"float32 D={D}")
 
 
 def test_out_buffer_and_errors(cuda_device):

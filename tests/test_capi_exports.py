@@ -77,11 +77,17 @@ def test_workspace_sizes_are_device_independent():
     # tensor-core shapes carry the norm-extension rows (32 B per point and per centroid)
     a = L.fkc_assign_workspace_size(1, 1000, 100, 128, 0)
     assert a >= 1000 * 32 + 100 * 32
-    # fp32 with D <= 128: plus the split bf16 operand rows (3D bf16 per point and centroid)
+    # fp32 with D <= 256: plus the split bf16 operand rows ([hi | lo], 2 * Dp bf16 per point
+    # and centroid, Dp = D rounded up to 64)
     al = lambda v: (v + 255) // 256 * 256
-    assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == a + al(1000 * 384 * 2) + al(
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == a + al(1000 * 256 * 2) + al(
+        100 * 256 * 2)
+    a144 = L.fkc_assign_workspace_size(1, 1000, 100, 144, 0)
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 144, 2) == a144 + al(1000 * 384 * 2) + al(
         100 * 384 * 2)
-    assert L.fkc_assign_workspace_size(1, 1000, 100, 144, 2) == 0  # fp32, D > 128: CUDA cores
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 272, 2) == 0  # fp32, D > 256: CUDA cores
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 512, 1) > 0   # bf16 up to D = 512
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 528, 1) == 0
     assert L.fkc_assign_workspace_size(1, 1000, 100, 100, 0) == 0  # D % 16 != 0
     u = L.fkc_update_workspace_size(2, 1000, 100)
     assert u >= 2 * (2 * 1000 * 4 + 2 * 100 * 4)
@@ -196,16 +202,21 @@ def test_lloyd_entry_points_check_arguments_on_the_host():
 
 
 def test_fp32_workspace_grows_with_the_split_rows():
-    """fp32 rows of D <= 128 add 3*D bf16 per point and per centroid to the Lloyd
-    workspace (the split operands of the tensor-core path); D > 128 does not."""
+    """fp32 rows of D <= 256 add 2 * Dp bf16 per point and per centroid to the Lloyd
+    workspace (the [hi | lo] split operands of the tensor-core path, Dp = D rounded up
+    to 64); D > 256 does not."""
     from flash_kmeans_cuda import _lib
 
     L = _lib.lib
     al = lambda v: (v + 255) // 256 * 256
+
     f16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 128, 0)
     f32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 128, 2)
-    # the rest of the layout is the same for both types
-    assert f32 - f16 == al(5000 * 384 * 2) + al(300 * 384 * 2)
-    w144_16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 144, 0)
-    w144_32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 144, 2)
-    assert w144_32 < w144_16  # fp32 D=144: no tensor-core rows at all
+    # the rest of the layout is the same for both types (both rows are 64..512 bytes)
+    assert f32 - f16 == al(5000 * 256 * 2) + al(300 * 256 * 2)
+    f16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 64, 0)
+    f32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 64, 2)
+    assert f32 - f16 == al(5000 * 128 * 2) + al(300 * 128 * 2)
+    w272_16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 272, 0)
+    w272_32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 272, 2)
+    assert w272_32 < w272_16  # fp32 D=272: no tensor-core rows at all

@@ -256,6 +256,7 @@ def run_pair(segs, MT, ST, NC, XS, own, nchunks):
 
 
 PAIR_CONFIGS = [
+    dict(MT=1, NC=64, ST=2, XS=1, own=False),    # 384 < D <= 512 (and split fp32, D > 192)
     dict(MT=1, NC=128, ST=2, XS=1, own=False),   # 256 < D <= 384
     dict(MT=2, NC=256, ST=8, XS=1, own=True),    # D <= 64 (pairs opted in)
     dict(MT=2, NC=256, ST=4, XS=1, own=False),   # D <= 128 (pairs opted in)
