@@ -292,6 +292,7 @@ def test_update_is_deterministic(cuda_device, dtype, B, N, K, D, zipf):
         st.step(c, nxt, True)
         torch.cuda.synchronize()
         outs.append((st.ids.clone(), st.counts.clone(), st.sums.clone(), nxt, st.shift.clone()))
+        st.set_centroids(c)  # the step left the norm terms of nxt in the workspace
         st.local(c)
         torch.cuda.synchronize()
         assert torch.equal(st.sums, outs[-1][2]), "sums of the local step differ from the step's"
