@@ -115,7 +115,8 @@ struct UpdateWorkspace {
   int32_t* offsets;     // (B, K) exclusive prefix of counts
   int32_t* cursor;      // (B, K) scatter cursors
   int32_t* perm;        // (B, N) row index in cluster order
-  int32_t* ids_sorted;  // (B, N) label in cluster order
+  int32_t* ids_sorted;  // (B, N) label in cluster order; follows perm directly (the
+                        // deterministic update stores (row, label) pairs over both)
   // Optional: zero_count floats at zero_f32 (16-byte aligned) are zeroed by the
   // scatter kernel after its dependency wait (saves a separate fill launch).
   float* zero_f32 = nullptr;

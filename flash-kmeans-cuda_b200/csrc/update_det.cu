@@ -18,8 +18,8 @@
 //   base     (det_base_kernel)    base[b][c][k] = offsets[b][k] + sum over the
 //            earlier chunks of hist[b][c'][k] (in place), offsets = exclusive
 //            scan of the counts (which the assignment kernel produced).
-//   scatter  (det_scatter_kernel) perm[base + rank] = row, ids_sorted likewise:
-//            a stable counting sort with no returning atomics.
+//   scatter  (det_scatter_kernel) sorted[base + rank] = {row, label}: a stable
+//            counting sort with no returning atomics, one 8-byte store per row.
 //   gather   (det_gather_kernel)  CTA spans of Pc sorted positions, cut into one
 //            span per group of L lanes (lane i holds 16-byte vector i of a row);
 //            each group walks its span with P row loads in flight and sums runs
@@ -90,7 +90,11 @@ DetGeom det_geom(int64_t N, int64_t K) {
 int64_t det_max_spans(int64_t B) { return kDetMaxSpans + B; }
 
 // ---------------------------------------------------------------------------
-// rank: stable ranks inside a chunk + the chunk's histogram.
+// rank: stable ranks inside a chunk + the chunk's histogram. A warp's rows are
+// taken in batches of kRankBatch 32-row steps whose labels are loaded together
+// (one memory round trip per batch), then counted step by step in order.
+constexpr int kRankBatch = 16;
+
 __global__ void __launch_bounds__(512) det_rank_kernel(const int32_t* __restrict__ ids, int N,
                                                        int K, int RW, int C,
                                                        int32_t* __restrict__ hist,
@@ -102,9 +106,9 @@ __global__ void __launch_bounds__(512) det_rank_kernel(const int32_t* __restrict
   const int b = blockIdx.x / C, c = blockIdx.x - b * C;
   {
     // zero the counters (independent of the previous kernel)
-    uint32_t* c32 = reinterpret_cast<uint32_t*>(cnt);
-    const int n32 = (W * K + 1) / 2;
-    for (int i = threadIdx.x; i < n32; i += blockDim.x) c32[i] = 0u;
+    uint4* c128 = reinterpret_cast<uint4*>(cnt);
+    const int n128 = (W * K * 2 + 15) / 16;
+    for (int i = threadIdx.x; i < n128; i += blockDim.x) c128[i] = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
   pdl_wait();
@@ -113,39 +117,58 @@ __global__ void __launch_bounds__(512) det_rank_kernel(const int32_t* __restrict
   const int r0 = c * (W * RW) + warp * RW;
   const int r1 = min(r0 + RW, N);
   uint16_t* my = cnt + warp * K;
-  for (int base = r0; base < r1; base += 32) {
-    const int row = base + lane;
-    int lab = row < r1 ? ids[rb + row] : -1;
-    if (lab >= K) lab = -1;  // never on this path (labels come from the assignment)
-    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, lab);
-    const int leader = __ffs(peers) - 1;
-    int old = 0;
-    if (lane == leader && lab >= 0) {
-      old = my[lab];
-      my[lab] = static_cast<uint16_t>(old + __popc(peers));
+  const uint32_t lt = lanemask_lt();
+  for (int base = r0; base < r1; base += 32 * kRankBatch) {
+    int lab[kRankBatch];
+#pragma unroll
+    for (int u = 0; u < kRankBatch; ++u) {
+      const int row = base + u * 32 + lane;
+      const int l = row < r1 ? ids[rb + row] : -1;
+      lab[u] = (l >= 0 && l < K) ? l : -1;  // labels come from the assignment: in [0, K)
     }
-    old = __shfl_sync(0xFFFFFFFFu, old, leader);
-    if (lab >= 0) rank[rb + row] = static_cast<uint16_t>(old + __popc(peers & lanemask_lt()));
+#pragma unroll
+    for (int u = 0; u < kRankBatch; ++u) {
+      const uint32_t peers = __match_any_sync(0xFFFFFFFFu, lab[u]);
+      const int leader = __ffs(peers) - 1;
+      int old = 0;
+      if (lane == leader && lab[u] >= 0) {
+        old = my[lab[u]];
+        my[lab[u]] = static_cast<uint16_t>(old + __popc(peers));
+      }
+      old = __shfl_sync(0xFFFFFFFFu, old, leader);
+      if (lab[u] >= 0)
+        rank[rb + base + u * 32 + lane] = static_cast<uint16_t>(old + __popc(peers & lt));
+    }
   }
   __syncthreads();
   // counters -> exclusive prefix over the warps (per label); chunk histogram
   int32_t* h = hist + (static_cast<int64_t>(b) * C + c) * K;
   for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    uint16_t v[16];
+#pragma unroll
+    for (int w = 0; w < 16; ++w) v[w] = w < W ? cnt[w * K + k] : 0;
     int run = 0;
-    for (int w = 0; w < W; ++w) {
-      const int v = cnt[w * K + k];
-      cnt[w * K + k] = static_cast<uint16_t>(run);
-      run += v;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      if (w < W) cnt[w * K + k] = static_cast<uint16_t>(run);
+      run += v[w];
     }
     h[k] = run;
   }
   __syncthreads();
-  for (int base = r0; base < r1; base += 32) {
-    const int row = base + lane;
-    if (row < r1) {
-      const int lab = ids[rb + row];
-      if (lab >= 0 && lab < K) rank[rb + row] = static_cast<uint16_t>(rank[rb + row] + my[lab]);
+  for (int base = r0; base < r1; base += 32 * kRankBatch) {
+    int lab[kRankBatch];
+    uint16_t rk[kRankBatch];
+#pragma unroll
+    for (int u = 0; u < kRankBatch; ++u) {
+      const int row = base + u * 32 + lane;
+      lab[u] = row < r1 ? ids[rb + row] : -1;
+      rk[u] = row < r1 ? rank[rb + row] : 0;
     }
+#pragma unroll
+    for (int u = 0; u < kRankBatch; ++u)
+      if (lab[u] >= 0 && lab[u] < K)
+        rank[rb + base + u * 32 + lane] = static_cast<uint16_t>(rk[u] + my[lab[u]]);
   }
 }
 
@@ -165,9 +188,27 @@ __global__ void __launch_bounds__(256) det_base_kernel(const int32_t* __restrict
   const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int32_t* cb = counts + static_cast<int64_t>(b) * K;
   int32_t* hb = hist + static_cast<int64_t>(b) * C * K;
-  // sum of the counts before this CTA's labels
+  // sum of the counts before this CTA's labels (kbeg is a multiple of 32: whole
+  // 16-byte vectors when the row of counts is 16-byte aligned)
   int s = 0;
-  for (int i = threadIdx.x; i < kbeg; i += 256) s += cb[i];
+  if ((reinterpret_cast<uintptr_t>(cb) & 15u) == 0) {
+    const int4* c4 = reinterpret_cast<const int4*>(cb);
+    const int n4 = kbeg / 4;
+    int i = threadIdx.x;
+    for (; i + 3 * 256 < n4; i += 4 * 256) {
+      int4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = c4[i + u * 256];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s += q[u].x + q[u].y + q[u].z + q[u].w;
+    }
+    for (; i < n4; i += 256) {
+      const int4 q = c4[i];
+      s += q.x + q.y + q.z + q.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < kbeg; i += 256) s += cb[i];
+  }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
   if (lane == 0) red[grp] = s;
@@ -210,11 +251,11 @@ __global__ void __launch_bounds__(256) det_base_kernel(const int32_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
-// scatter: perm[base[b][chunk][label] + rank] = row (stable counting sort).
+// scatter: sorted[base[b][chunk][label] + rank] = {row, label} (stable counting sort).
 __global__ void __launch_bounds__(256) det_scatter_kernel(
     const int32_t* __restrict__ ids, const uint16_t* __restrict__ rank,
-    const int32_t* __restrict__ base, int32_t* __restrict__ perm,
-    int32_t* __restrict__ ids_sorted, int N, int K, int R, int C, int64_t total) {
+    const int32_t* __restrict__ base, int2* __restrict__ sorted, int N, int K, int R, int C,
+    int64_t total) {
   pdl_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -225,9 +266,7 @@ __global__ void __launch_bounds__(256) det_scatter_kernel(
     if (lab < 0 || lab >= K) continue;
     const int pos = base[(static_cast<int64_t>(b) * C + n / R) * K + lab] + rank[i];
     if (pos < 0 || pos >= N) continue;  // counts inconsistent with the labels: drop, never overrun
-    const int64_t d = static_cast<int64_t>(b) * N + pos;
-    perm[d] = n;
-    ids_sorted[d] = lab;
+    sorted[static_cast<int64_t>(b) * N + pos] = make_int2(n, lab);
   }
 }
 
@@ -278,9 +317,8 @@ struct SpanEnds {
 
 template <typename T, int L, int P>
 __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
-    const T* __restrict__ x, const int32_t* __restrict__ perm,
-    const int32_t* __restrict__ ids_sorted, float* __restrict__ sums, float* __restrict__ part,
-    int N, int K, int Pc, int ncta_per_batch, int64_t total_spans) {
+    const T* __restrict__ x, const int2* __restrict__ sorted, float* __restrict__ sums,
+    float* __restrict__ part, int N, int K, int Pc, int ncta_per_batch, int64_t total_spans) {
   constexpr int kVec = 16 / sizeof(T);
   constexpr int G = 32 / L;
   constexpr int NG = kGatherWarps * G;  // group spans per CTA span
@@ -306,15 +344,12 @@ __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
     // meta of positions m .. m + L - 1 (lane i: position m + i)
     auto load_meta = [&](int m, int& lab, int& src) {
       const int q = m + i;
-      int l = q < p1 ? ids_sorted[rb + q] : -1;
-      if (l >= K) l = -1;
-      int s = l >= 0 ? perm[rb + q] : 0;
-      if (s < 0 || s >= N) {  // never on this path; a bad index reads nothing
-        l = -1;
-        s = 0;
-      }
-      lab = l;
-      src = s;
+      const int2 e = q < p1 ? __ldg(sorted + rb + q) : make_int2(0, -1);
+      // labels outside [0, K) or rows outside [0, N) never occur on this path; such
+      // an entry would read nothing
+      const bool ok = e.y >= 0 && e.y < K && e.x >= 0 && e.x < N;
+      lab = ok ? e.y : -1;
+      src = ok ? e.x : 0;
     };
     auto at = [&](int v, int jj) { return __shfl_sync(gmask, v, g * L + jj); };
     int labA, srcA, labB, srcB;
@@ -330,7 +365,6 @@ __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
 #pragma unroll
     for (int v = 0; v < kVec; ++v) acc[v] = 0.f;
     int cur = -1, run_start = p0;
-    bool first_done = false;  // the run touching p0 has been handed to shared memory
     // Hands a finished run over: whole cluster -> sums row; run at the span
     // start -> shared memory (first), run at the span end -> shared memory (last).
     auto flush = [&](bool at_end) {
@@ -340,7 +374,6 @@ __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
         store_row(sums + (static_cast<int64_t>(b) * K + cur) * D + i * kVec, acc);
       } else if (at_start) {
         store_row(&first_acc[j][i * kVec], acc);
-        first_done = true;
       } else {
         store_row(&last_acc[j][i * kVec], acc);
       }
@@ -382,7 +415,6 @@ __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
         flush(true);
       }
     }
-    (void)first_done;
     if (i == 0 && g * L + i == lane) {
       ends[j].first_lab = first_lab;
       ends[j].last_lab = last_lab;
@@ -393,8 +425,8 @@ __global__ void __launch_bounds__(kGatherThreads, 4) det_gather_kernel(
     constexpr int kCols = D / 4;
     if (static_cast<int>(threadIdx.x) < kCols) {
       const int t = threadIdx.x;
-      const int lab_before = S0 > 0 ? ids_sorted[rb + S0 - 1] : -1;
-      const int lab_after = S1 < N ? ids_sorted[rb + S1] : -1;
+      const int lab_before = S0 > 0 ? sorted[rb + S0 - 1].y : -1;
+      const int lab_after = S1 < N ? sorted[rb + S1].y : -1;
       int c_lab = -1;
       bool c_start = false;  // the carried run began at the CTA span start
       float4 c_acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -463,6 +495,8 @@ __global__ void __launch_bounds__(256) det_fixup_kernel(
     const int64_t kg = u0 + g;
     if (kg >= BK) continue;  // whole groups only: the shuffles below stay inside the group
     const int cnt = counts[kg];
+    uint4 ov = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (FINAL) ov = *reinterpret_cast<const uint4*>(old_c + kg * D + i * kVec);
     float acc[kVec];
 #pragma unroll
     for (int v = 0; v < kVec; ++v) acc[v] = 0.f;
@@ -522,7 +556,6 @@ __global__ void __launch_bounds__(256) det_fixup_kernel(
     if (write) store_row(srow, acc);
     if constexpr (FINAL) {
       const int64_t row = kg * D + i * kVec;
-      const uint4 ov = *reinterpret_cast<const uint4*>(old_c + row);
       const T* o = reinterpret_cast<const T*>(&ov);
       uint4 nvv;
       T* nv = reinterpret_cast<T*>(&nvv);
@@ -564,6 +597,10 @@ __global__ void __launch_bounds__(256) det_fixup_kernel(
     }
   }
 }
+
+// The sorted {row, label} pairs occupy the update workspace's perm and ids_sorted
+// arrays (adjacent, 256-byte aligned, each B*N int32 rounded up to 256 bytes).
+int2* det_sorted(const UpdateWorkspace& uw) { return reinterpret_cast<int2*>(uw.perm); }
 
 int det_sm_count() {
   const DeviceInfo* di = nullptr;
@@ -627,8 +664,7 @@ int launch_det_typed(const void* x, const int32_t* counts, const UpdateWorkspace
               static_cast<long long>(spans));
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(spans, res));
   FKC_TRY(launch_pdl(gk, dim3(grid), dim3(kGatherThreads), 0, stream, static_cast<const T*>(x),
-                     static_cast<const int32_t*>(uw.perm),
-                     static_cast<const int32_t*>(uw.ids_sorted), sums, dw.part,
+                     static_cast<const int2*>(det_sorted(uw)), sums, dw.part,
                      static_cast<int>(N), static_cast<int>(K), pc, static_cast<int>(ncta), spans));
   const int64_t BK = B * K;
   const int64_t blocks = std::min<int64_t>((BK + 8 * G - 1) / (8 * G), det_sm_count() * 8ll);
@@ -724,8 +760,8 @@ int launch_det_update(const void* x, const int32_t* ids, const int32_t* counts,
   const int64_t sblocks = std::min<int64_t>((total + 255) / 256, det_sm_count() * 16ll);
   FKC_TRY(launch_pdl(det_scatter_kernel, dim3(static_cast<unsigned>(sblocks)), dim3(256), 0, stream,
                      ids, static_cast<const uint16_t*>(dw.rank),
-                     static_cast<const int32_t*>(dw.hist), uw.perm, uw.ids_sorted,
-                     static_cast<int>(N), static_cast<int>(K), g.R, g.C, total));
+                     static_cast<const int32_t*>(dw.hist), det_sorted(uw), static_cast<int>(N),
+                     static_cast<int>(K), g.R, g.C, total));
   switch (dtype) {
     case FKC_DTYPE_F16:
       return launch_det_dtype<__half>(x, counts, uw, dw, sums, old_c, new_c, c_sq, cext, shift, B,
