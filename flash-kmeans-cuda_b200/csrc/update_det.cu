@@ -68,20 +68,25 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 // Chunk geometry of the stable counting sort (same on host and device).
 struct DetGeom {
   int W;   // warps (counter rows) per chunk CTA: W * K uint16 counters <= 128 KB
-  int RW;  // rows per warp (a multiple of 32, <= 32768 so uint16 counts never overflow)
-  int R;   // rows per chunk = W * RW (<= 65536, so in-chunk ranks fit uint16)
+  int RW;  // rows per warp (a multiple of 32)
+  int R;   // rows per chunk = W * RW <= 32768: ranks, prefixes and totals fit 16 bits
   int C;   // chunks per batch element
 };
 
-DetGeom det_geom(int64_t N, int64_t K) {
+// About kRankChunks chunk CTAs per call (one wave on 148 SMs), each at least
+// 64 rows per warp; at most 32768 rows per chunk, so that ranks, warp prefixes
+// and chunk totals all fit 16 bits.
+constexpr int64_t kRankChunks = 128;
+constexpr int64_t kRankMaxRows = 32768;
+
+DetGeom det_geom(int64_t B, int64_t N, int64_t K) {
   DetGeom g;
   g.W = K <= 4096 ? 16 : static_cast<int>(65536 / K);
   if (g.W < 1) g.W = 1;
-  // about K / W rows per warp, so the chunk histograms hold about as many
-  // entries as there are rows
-  int64_t rw = std::max<int64_t>(256, (K + g.W - 1) / g.W);
-  rw = (rw + 31) / 32 * 32;
-  g.RW = static_cast<int>(std::min<int64_t>(rw, 32768));
+  const int64_t per_batch = std::max<int64_t>(1, (kRankChunks + B - 1) / B);
+  int64_t rw = (N + per_batch * g.W - 1) / (per_batch * g.W);
+  rw = std::max<int64_t>(64, (rw + 31) / 32 * 32);
+  g.RW = static_cast<int>(std::min<int64_t>(rw, kRankMaxRows / g.W / 32 * 32));
   g.R = g.W * g.RW;
   g.C = static_cast<int>((N + g.R - 1) / g.R);
   return g;
@@ -141,19 +146,43 @@ __global__ void __launch_bounds__(512) det_rank_kernel(const int32_t* __restrict
     }
   }
   __syncthreads();
-  // counters -> exclusive prefix over the warps (per label); chunk histogram
+  // counters -> exclusive prefix over the warps (per label); chunk histogram.
+  // With K % 8 == 0 a thread takes 8 labels at once: 16-byte rows of packed
+  // 16-bit counters, added as 32-bit pairs (a prefix is below R <= 65536, so no
+  // carry crosses a half).
   int32_t* h = hist + (static_cast<int64_t>(b) * C + c) * K;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    uint16_t v[16];
-#pragma unroll
-    for (int w = 0; w < 16; ++w) v[w] = w < W ? cnt[w * K + k] : 0;
-    int run = 0;
-#pragma unroll
-    for (int w = 0; w < 16; ++w) {
-      if (w < W) cnt[w * K + k] = static_cast<uint16_t>(run);
-      run += v[w];
+  if ((K & 7) == 0) {
+    const int K8 = K / 8;
+    uint4* c8 = reinterpret_cast<uint4*>(cnt);
+    for (int k8 = threadIdx.x; k8 < K8; k8 += blockDim.x) {
+      uint4 run = make_uint4(0u, 0u, 0u, 0u);
+      for (int w = 0; w < W; ++w) {
+        const uint4 v = c8[w * K8 + k8];
+        c8[w * K8 + k8] = run;
+        run.x += v.x;
+        run.y += v.y;
+        run.z += v.z;
+        run.w += v.w;
+      }
+      const uint32_t q[4] = {run.x, run.y, run.z, run.w};
+      int4 lo, hi;
+      lo.x = static_cast<int>(q[0] & 0xFFFFu); lo.y = static_cast<int>(q[0] >> 16);
+      lo.z = static_cast<int>(q[1] & 0xFFFFu); lo.w = static_cast<int>(q[1] >> 16);
+      hi.x = static_cast<int>(q[2] & 0xFFFFu); hi.y = static_cast<int>(q[2] >> 16);
+      hi.z = static_cast<int>(q[3] & 0xFFFFu); hi.w = static_cast<int>(q[3] >> 16);
+      reinterpret_cast<int4*>(h)[2 * k8] = lo;
+      reinterpret_cast<int4*>(h)[2 * k8 + 1] = hi;
     }
-    h[k] = run;
+  } else {
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      int run = 0;
+      for (int w = 0; w < W; ++w) {
+        const int v = cnt[w * K + k];
+        cnt[w * K + k] = static_cast<uint16_t>(run);
+        run += v;
+      }
+      h[k] = run;
+    }
   }
   __syncthreads();
   for (int base = r0; base < r1; base += 32 * kRankBatch) {
@@ -708,7 +737,7 @@ int launch_det_dtype(const void* x, const int32_t* counts, const UpdateWorkspace
 
 size_t det_update_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   if (!det_shape_ok(N, K, D, dtype)) return 0;
-  const DetGeom g = det_geom(N, K);
+  const DetGeom g = det_geom(B, N, K);
   return align_up(static_cast<size_t>(B * N) * 2, 256) +
          align_up(static_cast<size_t>(B) * g.C * K * 4, 256) +
          align_up(static_cast<size_t>(det_max_spans(B)) * 2 * D * 4, 256);
@@ -717,7 +746,7 @@ size_t det_update_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
 DetWorkspace carve_det(void* ws, int64_t B, int64_t N, int64_t K, int64_t D, int dtype) {
   DetWorkspace w{};
   if (!det_shape_ok(N, K, D, dtype)) return w;
-  const DetGeom g = det_geom(N, K);
+  const DetGeom g = det_geom(B, N, K);
   uint8_t* p = static_cast<uint8_t*>(ws);
   w.rank = reinterpret_cast<uint16_t*>(p);
   p += align_up(static_cast<size_t>(B * N) * 2, 256);
@@ -740,8 +769,8 @@ int launch_det_update(const void* x, const int32_t* ids, const int32_t* counts,
                       int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
                       cudaStream_t stream) {
   FKC_REQUIRE(B * N <= 2147483647ll && B * K <= 2147483647ll, "update: sizes out of range");
-  const DetGeom g = det_geom(N, K);
-  FKC_REQUIRE(g.R <= 65536, "update: chunk of %d rows", g.R);
+  const DetGeom g = det_geom(B, N, K);
+  FKC_REQUIRE(g.R <= kRankMaxRows && g.RW >= 32, "update: chunk of %d rows", g.R);
   // rank + chunk histograms
   const size_t smem = align_up(static_cast<size_t>(g.W) * K * 2, 16);
   if (smem > 48 * 1024)
