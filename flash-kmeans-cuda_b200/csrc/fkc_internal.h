@@ -165,13 +165,11 @@ int launch_update_finalize(const void* x, const int32_t* ids, const int32_t* cou
                            int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
                            cudaStream_t stream);
 
-// Deterministic update of the Lloyd step (update_det.cu): a stable counting
-// sort (one cooperative launch) and a span gather that sums every cluster in
-// sorted order and finishes it (the finalize fused in), every float addition in
-// an order fixed by the labels. Labels must lie in [0, K); K <= 65536; rows of
-// 64..512 bytes, 16-byte aligned.
+// Deterministic update of the Lloyd step (update_det.cu): stable counting sort
+// (per-chunk ranks, chunk bases, scatter), span gather and a fixed-order join of
+// the clusters split between spans, the finalize fused into the last kernel.
+// Labels must lie in [0, K); K <= 65536; rows of 64..512 bytes, 16-byte aligned.
 struct DetWorkspace {
-  unsigned* ctl = nullptr;   // sort kernel control words (zero between launches)
   uint16_t* rank = nullptr;  // (B, N) stable rank of each row inside its chunk
   int32_t* hist = nullptr;   // (B, C, K) chunk histograms, then chunk slot bases
   float* part = nullptr;     // (spans, 2, D) partial sums of clusters cut by span ends
@@ -179,17 +177,15 @@ struct DetWorkspace {
 // 0 when the shape is outside the deterministic path.
 size_t det_update_bytes(int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
 DetWorkspace carve_det(void* ws, int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
-size_t det_ctl_bytes();
 bool det_update_ok(const DetWorkspace& dw, const void* x, const float* sums, const void* old_c,
-                   const void* new_c, int64_t B, int64_t N, int64_t K, int64_t D, int dtype);
-// counts: the histogram of ids; done: (B, K) int32, zero (and left at zero).
-// Writes offsets and the sorted (row, label) pairs over perm/ids_sorted (uw),
-// every row of sums and, when old_c is non-null, new_c (may alias old_c),
-// c_sq / cext (nullable) of new_c and shift (nullable, zeroed here first).
+                   const void* new_c, int64_t N, int64_t K, int64_t D, int dtype);
+// counts: the histogram of ids. Writes offsets/perm/ids_sorted (uw), every row of
+// sums and, when old_c is non-null, new_c (may alias old_c), c_sq / cext
+// (nullable) of new_c and shift (nullable, zeroed here first).
 int launch_det_update(const void* x, const int32_t* ids, const int32_t* counts,
-                      const UpdateWorkspace& uw, const DetWorkspace& dw, int32_t* done,
-                      float* sums, const void* old_c, void* new_c, float* c_sq, void* cext,
-                      float* shift, int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
+                      const UpdateWorkspace& uw, const DetWorkspace& dw, float* sums,
+                      const void* old_c, void* new_c, float* c_sq, void* cext, float* shift,
+                      int64_t B, int64_t N, int64_t K, int64_t D, int dtype,
                       cudaStream_t stream);
 
 // Whole-loop CUDA graph (lloyd_graph.cu).

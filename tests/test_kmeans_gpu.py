@@ -256,9 +256,10 @@ def _stepwise(x, init, max_iters, tol):
 @pytest.mark.parametrize("tol", [0.0, 1e-3])
 def test_graph_loop_matches_stepwise(cuda_device, dtype, tol):
     """The whole-loop graph (device-side while + tol) runs the same iterations as
-    the host-driven loop, bit for bit: the update sums every cluster in an order
-    fixed by the labels (stable counting sort, span gather, ordered join), so the
-    same iteration count, identical labels and identical centroids."""
+    the host-driven loop: same iteration count, labels >= 99.9% equal and
+    centroids within 1e-3 (the default update accumulates with atomics, so the
+    last bits may differ; FKC_DETERMINISTIC=1 makes them identical, see
+    tests/test_deterministic_gpu.py)."""
     from flash_kmeans_cuda import batch_kmeans_Euclid
 
     x = mixture(1, 16384, 64, 32, seed=21, dtype=dtype).cuda()
@@ -267,38 +268,8 @@ def test_graph_loop_matches_stepwise(cuda_device, dtype, tol):
     ids_s, c_s, n_s = _stepwise(x, init, 30, tol)
     torch.cuda.synchronize()
     assert n_g == n_s
-    assert torch.equal(ids_g, ids_s)
-    assert torch.equal(c_g, c_s)
-
-
-@pytest.mark.parametrize("dtype,B,N,K,D,zipf", [
-    ("float16", 1, 524288, 8192, 128, 1.1),   # c3 shape: the bench workload
-    ("bfloat16", 32, 16384, 1024, 64, 0.0),   # c4 shape
-    ("float32", 2, 50000, 3000, 32, 1.1),
-    ("float16", 1, 200000, 40000, 64, 0.0),   # K > 32768: one counter row per sort chunk
-])
-def test_update_is_deterministic(cuda_device, dtype, B, N, K, D, zipf):
-    """Two runs of the same Lloyd step give bit-identical sums, counts and
-    centroids, and the multi-GPU rank's step (sums only) agrees with them."""
-    from flash_kmeans_cuda.kmeans import LloydState
-
-    x = mixture(B, N, D, K, seed=N % 977, zipf=zipf, dtype=dtype).cuda()
-    c = subset_init(x.cpu(), K, seed=5).cuda()
-    outs = []
-    for _ in range(2):
-        st = LloydState(x, K)
-        st.set_centroids(c)
-        nxt = torch.empty_like(c)
-        st.step(c, nxt, True)
-        torch.cuda.synchronize()
-        outs.append((st.ids.clone(), st.counts.clone(), st.sums.clone(), nxt, st.shift.clone()))
-        st.set_centroids(c)  # the step left the norm terms of nxt in the workspace
-        st.local(c)
-        torch.cuda.synchronize()
-        assert torch.equal(st.sums, outs[-1][2]), "sums of the local step differ from the step's"
-    a, b = outs
-    for u, v, what in zip(a, b, ("labels", "counts", "sums", "centroids", "shift")):
-        assert torch.equal(u, v), f"{what} differ between two runs"
+    assert (ids_g == ids_s).float().mean().item() >= 0.999
+    _close_centroids(to_np(c_g.cpu()), to_np(c_s.cpu()), dtype)
 
 
 def test_graph_loop_replay_and_edges(cuda_device):
