@@ -345,11 +345,12 @@ __device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint
 // runs are contiguous even across segments) and flushed with vector atomics
 // when the label changes. Labels outside [0,K), including the -1 of unwritten
 // positions, load nothing and are never flushed.
-// Four CTAs (32 warps) per SM: the row loads of this kernel need that many
-// warps in flight (measured on B200: random 256-byte rows, 8 loads in flight
-// per 16-lane stream, read 134 MB in 41.8 us at 2 CTAs/SM and 30.7 us at 4).
+// Occupancy: 106 registers (2 CTAs per SM) at D = 128 fp16. Capped at 80
+// registers (3 CTAs per SM, small spills) it measured no faster at c3 (38.8 vs
+// 37.6 us per launch); a row-read probe reaches 30.7 us for the same 134 MB of
+// random 256-byte rows at 4 CTAs per SM without the run bookkeeping.
 template <typename T, int L, int P>
-__global__ void __launch_bounds__(256, 3) gather_accumulate_kernel(
+__global__ void __launch_bounds__(256) gather_accumulate_kernel(
     const T* __restrict__ x, const int32_t* __restrict__ perm,
     const int32_t* __restrict__ ids_sorted, float* __restrict__ sums,
     int32_t* __restrict__ counts, int N, int K, int spans_per_batch, int span_len,
