@@ -10,12 +10,13 @@
 //
 // Scoring. The MMA computes, per (row, centroid),
 //     acc = x.c - 0.5*||x||^2 - 0.5*||c||^2 - delta = -0.5 * ||x - c||^2 - delta
-// The norm terms enter through one extra K=16 slice of bf16 operands:
-//     A_ext[row] = {h1(x), h2(x), h3(x), 1, 1, 1, -delta(x), 0...}
-//     B_ext[k]   = {1, 1, 1, h1(c), h2(c), h3(c), 1, 0...}
-// where h1+h2+h3 is a three-term bf16 split (24 significant bits) of
+// The norm terms enter through one extra K=8 slice of tf32 operands (one
+// kind::tf32 MMA, half the cycles of a K=16 fp16 step):
+//     A_ext[row] = {h1(x), h2(x), h3(x), 1, 1, 1, -delta(x), 0}
+//     B_ext[k]   = {1, 1, 1, h1(c), h2(c), h3(c), 1, 0}
+// where h1+h2+h3 is a three-term tf32 split (33 significant bits) of
 // -0.5*||.||^2 and delta = 2^-12 ||x||^2 (+ 2^-100) is a row-constant bias
-// (norm_ext.cu). So TMEM holds -dist/2 - delta directly: no per-column c_sq
+// (fkc_common.cuh, norm_ext.cu). So TMEM holds -dist/2 - delta directly: no per-column c_sq
 // load and no FMA in the epilogue, and the score is strictly negative whenever
 // c_sq is the centroids' own norm (the fp32 accumulation rounds at ~2^-22 ||x||^2).
 //
@@ -77,7 +78,7 @@ using namespace fkc::ptx;
 constexpr int kRowsPerSub = 128;  // UMMA M per CTA (one TMEM lane per row)
 constexpr int kKBlockElems = 64;  // elements of one 128-byte swizzle row (16-bit types)
 constexpr int kKBlockBytes = 128;
-constexpr int kExtBytes = kNormExtBytes;  // 16 bf16 of the norm slice
+constexpr int kExtBytes = kNormExtBytes;  // 8 tf32 of the norm slice
 // Epilogue warps: two per TMEM lane quarter (= per SM sub-partition). Measured
 // on B200 at c3 (assign ms, single CTA): 8 warps 0.894, 16 warps 0.950 (more
 // issue overhead per score); without any epilogue the single-CTA MMA/TMA
@@ -320,6 +321,15 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
     umma_f16(d, a, b, idesc, acc);
 }
 
+// The norm slice: one K = 8 tf32 MMA (half the cycles of a K = 16 f16 step).
+template <int CG>
+__device__ __forceinline__ void mma_norm(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc) {
+  if constexpr (CG == 2)
+    umma_tf32_cg2(d, a, b, idesc, 1u);
+  else
+    umma_tf32(d, a, b, idesc, 1u);
+}
+
 // MMA completion -> barrier `bar` of this CTA, and of the peer CTA for CG = 2.
 template <int CG>
 __device__ __forceinline__ void mma_done(uint32_t bar) {
@@ -551,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     if (lane == 0 && leader) {
       const uint32_t idesc = umma_idesc_f16(BF16 ? 1u : 0u, CG * kRowsPerSub, NC);
-      const uint32_t idesc_ext = umma_idesc_f16(1u, CG * kRowsPerSub, NC);
+      const uint32_t idesc_ext = umma_idesc_tf32(CG * kRowsPerSub, NC);
       constexpr uint32_t kHi128 = umma_desc_hi(1024, kLayoutSwizzle128B);
       constexpr uint32_t kHi32 = umma_desc_hi(256, kLayoutSwizzle32B);
       uint32_t c_it = 0, x_it = 0, item = 0;
@@ -618,9 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
             }
-            mma<CG>(d_tmem, umma_desc(umma_desc_lo(sb + C::kOffAext + xi * C::kAextSubBytes), kHi32),
-                    umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
-                    idesc_ext, 1u);
+            mma_norm<CG>(d_tmem,
+                         umma_desc(umma_desc_lo(sb + C::kOffAext + xi * C::kAextSubBytes), kHi32),
+                         umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
+                         idesc_ext);
             mma_done<CG>(C::acc_full(sb, slot));
             if (ch == ch1 - 1) mma_done<CG>(C::x_empty(sb, xi));
             ++item;
@@ -969,12 +980,12 @@ int launch_tc_impl(const void* x, const void* centroids, const void* aext, const
   const uint64_t es = 2;
   FKC_TRY(encode_tmap_3d(&tm_x, tdt, x, D, N, B, D * es, N * D * es, kKBlockElems, kRowsPerSub,
                          CU_TENSOR_MAP_SWIZZLE_128B));
-  FKC_TRY(encode_tmap_3d(&tm_aext, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, aext, 16, N, B, kExtBytes,
-                         N * kExtBytes, 16, kRowsPerSub, CU_TENSOR_MAP_SWIZZLE_32B));
+  FKC_TRY(encode_tmap_3d(&tm_aext, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, aext, 8, N, B, kExtBytes,
+                         N * kExtBytes, 8, kRowsPerSub, CU_TENSOR_MAP_SWIZZLE_32B));
   FKC_TRY(encode_tmap_3d(&tm_c, tdt, centroids, D, K, B, D * es, K * D * es, kKBlockElems,
                          C::kNB, CU_TENSOR_MAP_SWIZZLE_128B));
-  FKC_TRY(encode_tmap_3d(&tm_cext, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cext, 16, K, B, kExtBytes,
-                         K * kExtBytes, 16, C::kNB, CU_TENSOR_MAP_SWIZZLE_32B));
+  FKC_TRY(encode_tmap_3d(&tm_cext, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, cext, 8, K, B, kExtBytes,
+                         K * kExtBytes, 8, C::kNB, CU_TENSOR_MAP_SWIZZLE_32B));
 
   const int64_t rows_per_tile = static_cast<int64_t>(CG) * MT * kRowsPerSub;
   const int64_t tiles_per_batch = (N + rows_per_tile - 1) / rows_per_tile;

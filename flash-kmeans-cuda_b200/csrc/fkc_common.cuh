@@ -39,41 +39,46 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
-constexpr int kNormExtBytes = 32;  // 16 bf16 per row
+constexpr int kNormExtBytes = 32;  // 8 tf32 (fp32 bit patterns) per row
 
-// v = h1 + h2 + h3 (+ < 2^-24 |v|), each term a bf16.
-__device__ __forceinline__ void split3_bf16(float v, uint32_t& h1, uint32_t& h2, uint32_t& h3) {
-  const __nv_bfloat16 b1 = __float2bfloat16_rn(v);
-  const float r1 = v - __bfloat162float(b1);
-  const __nv_bfloat16 b2 = __float2bfloat16_rn(r1);
-  const float r2 = r1 - __bfloat162float(b2);
-  const __nv_bfloat16 b3 = __float2bfloat16_rn(r2);
-  h1 = __bfloat16_as_ushort(b1);
-  h2 = __bfloat16_as_ushort(b2);
-  h3 = __bfloat16_as_ushort(b3);
+// x rounded to tf32 (the top 19 bits of an fp32: 10 stored mantissa bits),
+// to nearest with ties away from zero; returned as an fp32 whose low 13 bits
+// are zero, so the tensor cores read it exactly.
+__device__ __forceinline__ float round_tf32(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// Row side (x):        {h1, h2, h3, 1, 1, 1, -delta, 0 x 9}
-// Centroid side (c):   {1, 1, 1, h1, h2, h3, 1,      0 x 9}
-// so that <row_ext, centroid_ext> = value(row) + value(centroid) - delta(row),
-// with value = -||.||^2 / 2 and delta = 2^-12 ||x||^2 + 2^-100 a row-constant
-// bias (it does not change a row's argmin) that keeps every score -dist/2 -
-// delta strictly negative, far above the fp32 rounding of the accumulation.
+// v = t1 + t2 + t3 (+ < 2^-33 |v|), each term a tf32 value.
+__device__ __forceinline__ void split3_tf32(float v, float& t1, float& t2, float& t3) {
+  t1 = round_tf32(v);
+  const float r1 = v - t1;  // exact: t1 is v with its low bits rounded
+  t2 = round_tf32(r1);
+  t3 = round_tf32(r1 - t2);
+}
+
+// The norm slice of the tensor-core assignment: one K = 8 tf32 MMA per item
+// adds <row_ext, centroid_ext> to x.c, with
+//   row side (x):      {t1, t2, t3, 1, 1, 1, -delta, 0}
+//   centroid side (c): {1, 1, 1, t1, t2, t3, 1,      0}
+// so that the sum is value(row) + value(centroid) - delta(row), value =
+// -||.||^2 / 2 and delta = 2^-12 ||x||^2 + 2^-100 a row-constant bias (it does
+// not change a row's argmin) that keeps every score -dist/2 - delta strictly
+// negative, far above the fp32 rounding of the accumulation.
 __device__ __forceinline__ void write_norm_ext(void* dst, float value, bool row_side) {
-  uint32_t h1, h2, h3;
-  split3_bf16(value, h1, h2, h3);
-  const uint32_t one = 0x3F80u;  // bf16 1.0
-  uint4 lo;
+  float t1, t2, t3;
+  split3_tf32(value, t1, t2, t3);
+  float4 lo, hi;
   if (row_side) {
     const float delta = fmaf(-value, 0x1p-11f, 0x1p-100f);
-    const uint32_t nd = __bfloat16_as_ushort(__float2bfloat16_rn(-delta));
-    lo = make_uint4(h1 | (h2 << 16), h3 | (one << 16), one | (one << 16), nd);
+    lo = make_float4(t1, t2, t3, 1.f);
+    hi = make_float4(1.f, 1.f, round_tf32(-delta), 0.f);
   } else {
-    lo = make_uint4(one | (one << 16), one | (h1 << 16), h2 | (h3 << 16), one);
+    lo = make_float4(1.f, 1.f, 1.f, t1);
+    hi = make_float4(t2, t3, 1.f, 0.f);
   }
-  uint4* d = reinterpret_cast<uint4*>(dst);
+  float4* d = reinterpret_cast<float4*>(dst);
   d[0] = lo;
-  d[1] = make_uint4(0u, 0u, 0u, 0u);
+  d[1] = hi;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -165,6 +165,17 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::tf32 (K = 8 per instruction).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on the mbarrier when every tcgen05 op issued so far by this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -253,6 +264,16 @@ __device__ __forceinline__ void tmem_dealloc_cg2(uint32_t taddr, uint32_t ncols)
                : "memory");
 }
 
+__device__ __forceinline__ void umma_tf32_cg2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_f16_cg2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                              uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -323,6 +344,16 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t in_bf16, uint32_t
          | (in_bf16 << 10)         // B format
          | ((n >> 3) << 17)        // N >> 3
          | ((m >> 4) << 24);       // M >> 4
+}
+
+// kind::tf32 instruction descriptor: tf32 A and B (format code 2), fp32
+// accumulator, K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(uint32_t m, uint32_t n) {
+  return (1u << 4)             // D format: F32
+         | (2u << 7)           // A format: TF32
+         | (2u << 10)          // B format: TF32
+         | ((n >> 3) << 17)    // N >> 3
+         | ((m >> 4) << 24);   // M >> 4
 }
 
 }  // namespace ptx

@@ -1,7 +1,8 @@
-// Norm-extension rows read by the tcgen05 assignment kernel (one extra K=16
-// slice of bf16 operands that folds the squared norms into the MMA, see
-// assign_tc.cu): per point {h1,h2,h3,1,1,1,-delta,0...} with h1+h2+h3 =
-// -||x||^2/2, per centroid {1,1,1,h1,h2,h3,1,0...} with h = -||c||^2/2.
+// Norm-extension rows read by the tcgen05 assignment kernel (one extra K=8
+// slice of tf32 operands that folds the squared norms into the MMA, see
+// assign_tc.cu and write_norm_ext in fkc_common.cuh): per point
+// {h1,h2,h3,1,1,1,-delta,0} with h1+h2+h3 = -||x||^2/2, per centroid
+// {1,1,1,h1,h2,h3,1,0} with h = -||c||^2/2; 32 bytes per row.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 

@@ -89,10 +89,11 @@ FKC_CAPI_EXPORT int fkc_selftest_wait_timeout(uint32_t timeout_us, fkc_stream_t 
  *   read only by the fp32 / odd-D fallback, which clamps distances at 0 as
  *   the reference's safe kernel does; the tensor-core path ignores it (as the
  *   reference's raw-distance mma path does).
- *   fp16/bf16 with D % 16 == 0 and D <= 384 run the tcgen05 kernel; so does
- *   fp32 with D % 16 == 0 and D <= 128 (x and c as split bf16 rows of 3D:
- *   hi.hi + hi.lo + lo.hi, ~2^-16 relative), when the workspace holds those
- *   rows (fkc_assign_workspace_size counts them); fp32 with a smaller or no
+ *   fp16/bf16 with D % 16 == 0 and D <= 512 run the tcgen05 kernel; so does
+ *   fp32 with D % 16 == 0 and D <= 256 (x and c as split bf16 rows [hi | lo]
+ *   of 2 Dp elements, Dp = D rounded up to 64; the kernel accumulates hi.hi +
+ *   hi.lo + lo.hi, ~2^-16 relative), when the workspace holds those rows
+ *   (fkc_assign_workspace_size counts them); fp32 with a smaller or no
  *   workspace keeps the CUDA-core kernel.
  * Replaces: _C.euclid_assign (csrc/bindings.cpp:43-71),
  *           fkc::euclid_assign_out (csrc/api.cpp:58-72),
@@ -202,6 +203,12 @@ FKC_CAPI_EXPORT int fkc_finalize(const float* sums, const int32_t* counts, const
  * The centroids passed to fkc_lloyd_local must be those last produced by
  * fkc_lloyd_finalize with the same workspace, or fkc_lloyd_set_centroids
  * must be called first (initial centroids).
+ * Reproducibility: with FKC_DETERMINISTIC=1 in the environment (read once),
+ * fkc_lloyd_update and fkc_lloyd_iter sum every cluster in an order fixed by
+ * the labels (labels in [0,K), K <= 65536, rows of 64..512 bytes, 16-byte
+ * aligned buffers), so repeated runs on one device give bit-identical sums
+ * and centroids; by default the sums accumulate with atomics (faster; equal
+ * up to fp32 rounding).
  * ---------------------------------------------------------------------- */
 FKC_CAPI_EXPORT size_t fkc_lloyd_workspace_size(int64_t B, int64_t N, int64_t K, int64_t D,
                                                 int dtype);

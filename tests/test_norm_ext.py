@@ -1,48 +1,56 @@
 """The norm slice of the tensor-core assignment, restated in numpy (no GPU).
 
-Every point row carries {h1,h2,h3,1,1,1,-delta,0...} and every centroid row
-{1,1,1,g1,g2,g3,1,0...} (bf16), with h1+h2+h3 = -||x||^2/2 and g1+g2+g3 = -||c||^2/2
-split into three bf16 terms (fkc_common.cuh: split3_bf16, write_norm_ext), and
-delta = 2^-11 * ||x||^2/2 + 2^-100. One extra K=16 MMA adds their dot product to
-x.c, so the fp32 accumulator holds -||x - c||^2/2 - delta: strictly negative, which the
-epilogue's packed keys (column index in the low mantissa bits, max over floats) need for
-ties to go to the lowest column."""
+Every point row carries {h1,h2,h3,1,1,1,-delta,0} and every centroid row
+{1,1,1,g1,g2,g3,1,0} (tf32 values stored as fp32 bit patterns, 32 bytes), with
+h1+h2+h3 = -||x||^2/2 and g1+g2+g3 = -||c||^2/2 split into three tf32 terms
+(fkc_common.cuh: round_tf32, split3_tf32, write_norm_ext), and delta =
+2^-11 * ||x||^2/2 + 2^-100 rounded to tf32. One extra K=8 tf32 MMA adds their dot
+product to x.c, so the fp32 accumulator holds -||x - c||^2/2 - delta: strictly
+negative, which the epilogue's packed keys (column index in the low mantissa bits,
+max over floats) need for ties to go to the lowest column."""
 
 from __future__ import annotations
 
 import numpy as np
 
 
-def bf16(v):
+def tf32(v):
+    """fp32 -> tf32 (round to nearest, ties away from zero) as an fp32 value."""
     u = np.asarray(v, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
-    return r.astype(np.uint32).view(np.float32)
+    r = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return r.view(np.float32)
 
 
 def split3(v):
     v = np.float32(v)
-    b1 = bf16(v)
-    r1 = np.float32(v - b1)
-    b2 = bf16(r1)
-    r2 = np.float32(r1 - b2)
-    b3 = bf16(r2)
-    return b1, b2, b3
+    t1 = tf32(v)
+    r1 = np.float32(v - t1)
+    t2 = tf32(r1)
+    t3 = tf32(np.float32(r1 - t2))
+    return t1, t2, t3
 
 
 def row_ext(sq):
     value = np.float32(-0.5) * np.float32(sq)
     h = split3(value)
     delta = np.float32(np.float32(-value) * np.float32(2.0 ** -11) + np.float32(2.0 ** -100))
-    return np.array([*h, 1, 1, 1, bf16(-delta)] + [0] * 9, dtype=np.float32)
+    return np.array([*h, 1, 1, 1, tf32(-delta), 0], dtype=np.float32)
 
 
 def cent_ext(sq):
     value = np.float32(-0.5) * np.float32(sq)
     g = split3(value)
-    return np.array([1, 1, 1, *g, 1] + [0] * 9, dtype=np.float32)
+    return np.array([1, 1, 1, *g, 1, 0], dtype=np.float32)
 
 
-def test_three_bf16_terms_carry_fp32_precision():
+def test_tf32_terms_are_exact_for_the_tensor_cores():
+    rng = np.random.default_rng(3)
+    for v in rng.standard_normal(2000).astype(np.float32) * np.float32(1e3):
+        for t in split3(v):
+            assert (np.asarray(t, dtype=np.float32).view(np.uint32) & 0x1FFF) == 0
+
+
+def test_three_tf32_terms_carry_fp32_precision():
     rng = np.random.default_rng(0)
     for v in rng.standard_normal(2000).astype(np.float32) * np.float32(1e4):
         s = sum(np.float64(t) for t in split3(v))
