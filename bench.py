@@ -534,16 +534,27 @@ def run_ours(args, w: dict) -> None:
             barrier_sync(dev)
             i = args.warmup + args.steps + r
             a, b = bufs[i % 2], bufs[(i + 1) % 2]
+            if mm is not None:
+                # the timed step: wait for the previous step's finalize everywhere, local
+                # step, finalize with the arrival barrier folded in
+                evs[0].record(stream)
+                mm.wait_previous()
+                evs[2].record(stream)
+                st.local(a)
+                evs[1].record(stream)
+                mm.reduce_finalize_synced(i, False)
+                evs[3].record(stream)
+                evs[4].record(stream)
+                torch.cuda.synchronize(dev)
+                if r == 0:
+                    continue
+                acc += torch.tensor([evs[2].elapsed_time(evs[1]), evs[0].elapsed_time(evs[2]),
+                                     evs[1].elapsed_time(evs[3]), 0.0], dtype=torch.float64) / 5
+                continue
             evs[0].record(stream)
             st.local(a)
             evs[1].record(stream)
-            if mm is not None:
-                mm._barrier()
-                evs[2].record(stream)
-                mm.reduce_finalize(i, False)
-                evs[3].record(stream)
-                mm._barrier()
-            elif w["shard"] == "N":
+            if w["shard"] == "N":
                 evs[2].record(stream)
                 allreduce_sums_counts(st.sums, st.counts)
                 evs[3].record(stream)
@@ -565,10 +576,12 @@ def run_ours(args, w: dict) -> None:
         rows = [t.tolist() for t in alls]
         if mm is not None:
             per_rank = {"local_ms": [r_[0] for r_ in rows],
-                        "barrier_ms": [r_[1] + r_[3] for r_ in rows],
+                        "step_wait_ms": [r_[1] for r_ in rows],
                         "reduce_finalize_ms": [r_[2] for r_ in rows],
-                        "path": "multicast finalize (fkc_lloyd_finalize_multimem) between two "
-                                "symmetric-memory barriers"}
+                        "path": "multicast finalize with the arrival barrier in the kernel "
+                                "(fkc_lloyd_finalize_multimem_synced) + the completion wait "
+                                "before the next local step (fkc_multimem_step_wait); "
+                                "reduce_finalize_ms includes waiting for the slowest rank"}
         else:
             per_rank = {"local_ms": [r_[0] for r_ in rows],
                         "allreduce_ms": [r_[2] for r_ in rows],

@@ -599,6 +599,38 @@ FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem(
                                   as_stream(stream));
 }
 
+FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem_synced(
+    const float* mc_sums, const int32_t* mc_counts, const void* centroids, void* mc_centroids,
+    void* mc_workspace, unsigned int* mc_shift, float* shift_clear, int64_t row_begin,
+    int64_t row_end, int64_t B, int64_t K, int64_t D, int dtype, unsigned int* bar,
+    unsigned int* mc_bar, uint32_t epoch, int world, fkc_stream_t stream) {
+  clear_error();
+  FKC_TRY(check_dims(B, 1, K, D, dtype));
+  FKC_REQUIRE(mc_sums && mc_counts && centroids && mc_centroids && mc_workspace && bar && mc_bar,
+              "null argument");
+  FKC_REQUIRE(world >= 1 && epoch >= 1, "world (%d) and epoch (%u) must be >= 1", world, epoch);
+  FKC_REQUIRE(row_begin >= 0 && row_begin < row_end && row_end <= B * K,
+              "rows [%lld, %lld) must be a non-empty part of [0, B*K=%lld)",
+              static_cast<long long>(row_begin), static_cast<long long>(row_end),
+              static_cast<long long>(B * K));
+  FKC_REQUIRE((reinterpret_cast<uintptr_t>(bar) & 3u) == 0 &&
+                  (reinterpret_cast<uintptr_t>(mc_bar) & 3u) == 0,
+              "barrier words must be 4-byte aligned");
+  LloydWs w;
+  FKC_TRY(carve_lloyd(mc_workspace, lloyd_ws_bytes(B, 1, K, D, dtype), B, 1, K, D, dtype, &w));
+  return launch_finalize_multimem(mc_sums, mc_counts, centroids, mc_centroids, w.c_sq, w.cext,
+                                  mc_shift, shift_clear, row_begin, row_end, D, dtype,
+                                  as_stream(stream), bar, mc_bar,
+                                  epoch * static_cast<uint32_t>(world));
+}
+
+FKC_CAPI_EXPORT int fkc_multimem_step_wait(const unsigned int* bar, uint32_t epoch, int world,
+                                           fkc_stream_t stream) {
+  clear_error();
+  FKC_REQUIRE(bar != nullptr && world >= 1, "bar must be non-null and world >= 1");
+  return launch_step_wait(bar, epoch * static_cast<uint32_t>(world), as_stream(stream));
+}
+
 FKC_CAPI_EXPORT int fkc_lloyd_run(const void* x, void* centroids, int32_t* ids, float* sums,
                                   int32_t* counts, float* shift, int32_t* n_iters, int max_iters,
                                   float tol, int64_t B, int64_t N, int64_t K, int64_t D,

@@ -17,6 +17,7 @@
 #include "fkc_common.cuh"
 #include "fkc_internal.h"
 #include "fkc_launch.cuh"
+#include "fkc_ptx.cuh"
 
 namespace fkc {
 namespace {
@@ -176,26 +177,81 @@ __device__ __forceinline__ uint32_t pack2(T a, T b) {
   return static_cast<uint32_t>(ua) | (static_cast<uint32_t>(ub) << 16);
 }
 
+__device__ __forceinline__ void mc_red_add_release_u32(unsigned int* mc, uint32_t v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned int* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Cross-GPU step barrier words (this rank's copies; the multicast address adds
+// to every rank's copy): [0] ranks arrived at the finalize of the step,
+// [1] ranks whose finalize of the step has completed, [2] finished CTAs of
+// this rank's finalize launch (local).
+enum : int { kBarArrive = 0, kBarDone = 1, kBarCtas = 2 };
+constexpr uint64_t kStepBarrierNs = 4000000000ull;
+enum : int { kErrStepBarrier = 141 };
+
+// Bounded wait until *word - target >= 0 (wrapping epoch counters); records
+// kErrStepBarrier in the device error word and returns false on timeout.
+__device__ bool wait_counter(const unsigned int* word, unsigned target, int* err) {
+  const uint64_t t0 = ptx::globaltimer_ns();
+  while (static_cast<int>(ld_acquire_sys(word) - target) < 0) {
+    if (ptx::globaltimer_ns() - t0 > kStepBarrierNs) {
+      if (err != nullptr) atomicCAS(err, 0, kErrStepBarrier);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 // D % 4 == 0: lane l owns elements [4l + 128i, 4l + 128i + 4) of the row.
+// With bar != nullptr the step's cross-GPU barriers are folded in: thread 0 of
+// CTA 0 adds this rank's arrival to every rank's bar[0] (multicast, release),
+// every CTA waits until bar[0] reaches epoch * world (all ranks' local sums and
+// counts are final), and the last CTA of the launch adds this rank's
+// completion to every rank's bar[1] after its multicast stores.
 template <typename T>
 __global__ void __launch_bounds__(256) finalize_multimem_kernel(
     const float* __restrict__ mc_sums, const int32_t* __restrict__ mc_counts,
     const T* __restrict__ old_c, T* mc_new_c, float* mc_c_sq, uint8_t* mc_cext,
-    unsigned int* mc_shift, float* shift_clear, int64_t row0, int64_t row1, int D) {
+    unsigned int* mc_shift, float* shift_clear, int64_t row0, int64_t row1, int D,
+    unsigned int* bar, unsigned int* mc_bar, unsigned target, int* err) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
+  __shared__ int go;
+  if (bar != nullptr) {
+    if (threadIdx.x == 0) {
+      if (blockIdx.x == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        mc_red_add_release_u32(mc_bar + kBarArrive, 1u);
+      }
+      go = wait_counter(bar + kBarArrive, target, err) ? 1 : 0;
+    }
+    __syncthreads();
+  } else if (threadIdx.x == 0) {
+    go = 1;
+  }
+  if (bar == nullptr) __syncthreads();
   if (shift_clear != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *shift_clear = 0.f;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = row0 + static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) +
                    (threadIdx.x >> 5);
-       r < row1; r += warps_total) {
+       go != 0 && r < row1; r += warps_total) {
+    // the sums reduction does not depend on the count: issue both before waiting
+    float4 sv0 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (4 * lane < D) sv0 = mc_ld_reduce_v4(mc_sums + r * D + 4 * lane);
     int32_t cnt = 0;
     if (lane == 0) cnt = static_cast<int32_t>(mc_ld_reduce_u32(mc_counts + r));
     cnt = __shfl_sync(0xFFFFFFFFu, cnt, 0);
     const float fc = static_cast<float>(cnt);
     float sq = 0.f, sh = 0.f;
     for (int d = 4 * lane; d < D; d += 128) {
-      const float4 sv = mc_ld_reduce_v4(mc_sums + r * D + d);
+      const float4 sv = d == 4 * lane ? sv0 : mc_ld_reduce_v4(mc_sums + r * D + d);
       const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
       T nv[4];
 #pragma unroll
@@ -232,6 +288,25 @@ __global__ void __launch_bounds__(256) finalize_multimem_kernel(
   // The multicast stores and reductions are ordered before whatever follows
   // this kernel on the stream (the cross-GPU barrier's release).
   asm volatile("fence.acq_rel.sys;" ::: "memory");
+  if (bar != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // the last CTA out signals this rank's completion to every rank
+      if (atomicAdd(bar + kBarCtas, 1u) == gridDim.x - 1) {
+        bar[kBarCtas] = 0u;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        mc_red_add_release_u32(mc_bar + kBarDone, 1u);
+      }
+    }
+  }
+}
+
+// Waits (bounded) until every rank's finalize of the previous step has
+// completed (bar[1] reaches target): before the next local step writes the
+// sums the other ranks read and reads the centroids they write.
+__global__ void step_wait_kernel(const unsigned int* bar, unsigned target, int* err) {
+  pdl_wait();
+  if (threadIdx.x == 0) wait_counter(bar + kBarDone, target, err);
 }
 
 __global__ void __launch_bounds__(256) zero_fill_kernel(uint32_t* __restrict__ p, int64_t words,
@@ -265,36 +340,48 @@ int launch_zero_fill(void* ptr, size_t bytes, cudaStream_t stream) {
                     static_cast<uint32_t*>(ptr), words, vec);
 }
 
+int launch_step_wait(const unsigned int* bar, unsigned target, cudaStream_t stream) {
+  return launch_pdl(step_wait_kernel, dim3(1), dim3(32), 0, stream, bar, target,
+                    device_error_word());
+}
+
 int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, const void* old_c,
                              void* mc_new_c, float* mc_c_sq, void* mc_cext,
                              unsigned int* mc_shift, float* shift_clear, int64_t row0,
-                             int64_t row1, int64_t D, int dtype, cudaStream_t stream) {
+                             int64_t row1, int64_t D, int dtype, cudaStream_t stream,
+                             unsigned int* bar, unsigned int* mc_bar, unsigned target) {
   FKC_REQUIRE(D % 4 == 0, "finalize_multimem: D must be a multiple of 4 (got %lld)",
               static_cast<long long>(D));
   const int64_t rows = row1 - row0;
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   int64_t grid = (rows + 7) / 8;
-  const int64_t cap = static_cast<int64_t>(di->sm_count) * 16;
+  // With the arrival barrier in the kernel every CTA waits for all ranks' CTA
+  // 0: keep the grid within one resident wave (4 CTAs of 256 threads and at
+  // most 48 registers per thread fit an SM), so CTA 0 is always running.
+  const int64_t cap = static_cast<int64_t>(di->sm_count) * (bar != nullptr ? 4 : 16);
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   uint8_t* ce = static_cast<uint8_t*>(mc_cext);
   const int d = static_cast<int>(D);
   const dim3 g(static_cast<unsigned>(grid)), blk(256);
+  int* err = bar != nullptr ? device_error_word() : nullptr;
   switch (dtype) {
     case FKC_DTYPE_F16:
       return launch_pdl(finalize_multimem_kernel<__half>, g, blk, 0, stream, mc_sums, mc_counts,
                         static_cast<const __half*>(old_c), static_cast<__half*>(mc_new_c),
-                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
+                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d, bar, mc_bar, target,
+                        err);
     case FKC_DTYPE_BF16:
       return launch_pdl(finalize_multimem_kernel<__nv_bfloat16>, g, blk, 0, stream, mc_sums,
                         mc_counts, static_cast<const __nv_bfloat16*>(old_c),
                         static_cast<__nv_bfloat16*>(mc_new_c), mc_c_sq, ce, mc_shift,
-                        shift_clear, row0, row1, d);
+                        shift_clear, row0, row1, d, bar, mc_bar, target, err);
     case FKC_DTYPE_F32:
       return launch_pdl(finalize_multimem_kernel<float>, g, blk, 0, stream, mc_sums, mc_counts,
                         static_cast<const float*>(old_c), static_cast<float*>(mc_new_c),
-                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d);
+                        mc_c_sq, ce, mc_shift, shift_clear, row0, row1, d, bar, mc_bar, target,
+                        err);
     default:
       return set_error(FKC_EINVAL, "finalize_multimem: bad dtype %d", dtype);
   }

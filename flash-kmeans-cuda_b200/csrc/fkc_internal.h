@@ -222,10 +222,16 @@ uint64_t capture_launch_count();
 
 // Rows [row0, row1) of the multi-GPU finalize over NVLink multicast (mc_*:
 // multicast addresses of symmetric buffers; old_c: this rank's copy).
+// bar (nullable): this rank's copy of the step's barrier words, mc_bar their
+// multicast address, target = epoch * world (see finalize.cu).
 int launch_finalize_multimem(const float* mc_sums, const int32_t* mc_counts, const void* old_c,
                              void* mc_new_c, float* mc_c_sq, void* mc_cext,
                              unsigned int* mc_shift, float* shift_clear, int64_t row0,
-                             int64_t row1, int64_t D, int dtype, cudaStream_t stream);
+                             int64_t row1, int64_t D, int dtype, cudaStream_t stream,
+                             unsigned int* bar = nullptr, unsigned int* mc_bar = nullptr,
+                             unsigned target = 0);
+// Bounded wait until bar[1] (ranks whose synced finalize completed) reaches target.
+int launch_step_wait(const unsigned int* bar, unsigned target, cudaStream_t stream);
 
 // shift_zeroed: *shift_out is already 0 (the scatter of this step zeroed it).
 int launch_finalize(const float* sums, const int32_t* counts, const void* old_c, void* new_c,

@@ -67,6 +67,10 @@ _SIGNATURES = {
                                c_i64, c_int, c_vp, c_size, c_vp]),
     "fkc_lloyd_finalize_multimem": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64,
                                             c_i64, c_i64, c_i64, c_i64, c_int, c_vp]),
+    "fkc_lloyd_finalize_multimem_synced": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                   c_i64, c_i64, c_i64, c_i64, c_i64, c_int,
+                                                   c_vp, c_vp, ctypes.c_uint32, c_int, c_vp]),
+    "fkc_multimem_step_wait": (c_int, [c_vp, ctypes.c_uint32, c_int, c_vp]),
     "fkc_lloyd_run": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, ctypes.c_float,
                               c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_size, c_vp]),
 }

@@ -161,7 +161,8 @@ class MultimemLloyd:
         off_counts = up(off_sums + B * K * D * 4)
         off_c = up(off_counts + B * K * 4)
         off_shift = up(off_c + B * K * D * es)
-        total = up(off_shift + 8)
+        off_bar = up(off_shift + 8)  # the step's barrier words (fkc_lloyd_finalize_multimem_synced)
+        total = up(off_bar + 16)
         self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
         self.handle = symm.rendezvous(self.buf, group if group is not None else dist.group.WORLD)
         mc = int(self.handle.multicast_ptr)
@@ -174,10 +175,13 @@ class MultimemLloyd:
         self.counts = b[off_counts:off_counts + B * K * 4].view(torch.int32).view(B, K)
         self.centroids = b[off_c:off_c + B * K * D * es].view(x_local.dtype).view(B, K, D)
         self.shift = b[off_shift:off_shift + 8].view(torch.float32)
+        self.bar = b[off_bar:off_bar + 16]
         self.mc_ws, self.mc_sums, self.mc_counts = mc + off_ws, mc + off_sums, mc + off_counts
-        self.mc_c, self.mc_shift = mc + off_c, mc + off_shift
+        self.mc_c, self.mc_shift, self.mc_bar = mc + off_c, mc + off_shift, mc + off_bar
+        self.epoch = 0  # steps run (the barrier words count arrivals per step)
         self.state = LloydState(x_local, K, ws=self.ws, sums=self.sums, counts=self.counts)
         rank, world = dist.get_rank(group), dist.get_world_size(group)
+        self.world = world
         self.rows = shard_bounds(B * K, world, rank)
         self.dims = (B, K, D, code)
         self._barrier()
@@ -188,10 +192,13 @@ class MultimemLloyd:
     def release(self) -> None:
         """Ends the symmetric-memory use: every rank passes a last barrier with
         no kernel of this object in flight before the buffer can be freed."""
+        self.wait_previous()
         self._barrier()
         torch.cuda.synchronize(self.buf.device)
 
     def set_centroids(self, c: torch.Tensor) -> None:
+        # the other ranks' last finalize may still be writing into these buffers
+        self.wait_previous()
         self.centroids.copy_(c)
         self.state.set_centroids(self.centroids)
 
@@ -211,13 +218,49 @@ class MultimemLloyd:
                 self.rows[0], self.rows[1], B, K, D, code, st._stream()),
                 "fkc_lloyd_finalize_multimem")
 
+    def wait_previous(self) -> None:
+        """Stream-ordered wait until every rank finished the previous step's finalize."""
+        from ._lib import check, lib
+
+        if self.epoch > 0:
+            with torch.cuda.device(self.state.device):
+                check(lib.fkc_multimem_step_wait(self.bar.data_ptr(), self.epoch, self.world,
+                                                 self.state._stream()), "fkc_multimem_step_wait")
+
+    def reduce_finalize_synced(self, it: int, want_shift: bool) -> None:
+        """reduce_finalize with the step's cross-GPU barriers folded into the kernel
+        (every rank arrives, waits for all, finalizes its rows, signals completion)."""
+        from ._lib import check, lib
+
+        p = it & 1
+        st = self.state
+        B, K, D, code = self.dims
+        self.epoch += 1
+        if self.rows[0] == self.rows[1]:
+            raise RuntimeError("synced multicast finalize needs at least one row per rank")
+        with torch.cuda.device(st.device):
+            check(lib.fkc_lloyd_finalize_multimem_synced(
+                self.mc_sums, self.mc_counts, self.centroids.data_ptr(), self.mc_c, self.mc_ws,
+                (self.mc_shift + 4 * p) if want_shift else None,
+                self.shift[1 - p:2 - p].data_ptr() if want_shift else None,
+                self.rows[0], self.rows[1], B, K, D, code, self.bar.data_ptr(), self.mc_bar,
+                self.epoch, self.world, st._stream()),
+                "fkc_lloyd_finalize_multimem_synced")
+
     def step(self, it: int, want_shift: bool) -> Optional[torch.Tensor]:
         """One iteration in place on ``self.centroids``; returns the (1,) shift
-        tensor when ``want_shift`` (valid once the stream reaches it)."""
-        self.state.local(self.centroids)
-        self._barrier()
-        self.reduce_finalize(it, want_shift)
-        self._barrier()
+        tensor when ``want_shift`` (valid once the stream reaches it). With at
+        least one centroid row per rank the two barriers of the step run inside
+        device code (no separate barrier launches)."""
+        if self.rows[0] < self.rows[1]:
+            self.wait_previous()
+            self.state.local(self.centroids)
+            self.reduce_finalize_synced(it, want_shift)
+        else:
+            self.state.local(self.centroids)
+            self._barrier()
+            self.reduce_finalize(it, want_shift)
+            self._barrier()
         p = it & 1
         return self.shift[p:p + 1] if want_shift else None
 

@@ -266,6 +266,31 @@ FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem(
     int64_t row_end, int64_t B, int64_t K, int64_t D, int dtype, fkc_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * fkc_lloyd_finalize_multimem with the step's two cross-GPU barriers folded
+ * into device code (no reference counterpart; the reference is single-GPU).
+ *   bar: this rank's copy of 3 uint32 words in the symmetric buffer (zero
+ *   before the first step), mc_bar: their multicast address; epoch: 1 for the
+ *   first step, +1 for each later one; world: ranks. Every rank must call it
+ *   once per step with the same epoch and a non-empty row range.
+ *   The kernel adds this rank's arrival to every rank's bar[0], waits until all
+ *   ranks have arrived (their local sums and counts are final), finalizes its
+ *   rows, and its last CTA adds this rank's completion to every rank's bar[1].
+ *   fkc_multimem_step_wait(bar, epoch, world) then waits, on the stream, until
+ *   every rank's finalize of step `epoch` has completed: call it before the
+ *   next local step (which overwrites the sums the ranks read and reads the
+ *   centroids they write).
+ *   Waits are bounded (4 s): on expiry the kernel records FKC_ETIMEOUT for
+ *   fkc_device_status() and returns instead of hanging.
+ * ---------------------------------------------------------------------- */
+FKC_CAPI_EXPORT int fkc_lloyd_finalize_multimem_synced(
+    const float* mc_sums, const int32_t* mc_counts, const void* centroids, void* mc_centroids,
+    void* mc_workspace, unsigned int* mc_shift, float* shift_clear, int64_t row_begin,
+    int64_t row_end, int64_t B, int64_t K, int64_t D, int dtype, unsigned int* bar,
+    unsigned int* mc_bar, uint32_t epoch, int world, fkc_stream_t stream);
+FKC_CAPI_EXPORT int fkc_multimem_step_wait(const unsigned int* bar, uint32_t epoch, int world,
+                                           fkc_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * The whole Lloyd loop (batch_kmeans_Euclid without init, kmeans.py:162-195)
  * as ONE CUDA graph launch: a device-side WHILE loop over in-place iterations
  * (assign -> update -> finalize) that stops after max_iters iterations or,
