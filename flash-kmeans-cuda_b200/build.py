@@ -122,6 +122,37 @@ def build_torch_api(force: bool = False) -> Path | None:
     return TORCH_API_LIB
 
 
+def build_py_module(force: bool = False) -> Path | None:
+    """The compiled ``flash_kmeans_cuda._C`` module (reference: flash_kmeans_cuda/csrc/bindings.cpp),
+    a PyTorch extension over the C-ABI of libfkc_b200.so."""
+    try:
+        import sysconfig
+
+        import torch
+        from torch.utils import cpp_extension
+    except Exception:  # pragma: no cover - torch is part of the image
+        return None
+    src = CSRC / "py_C.cpp"
+    out = OUT_DIR / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if not (force or _newer(out, [src, INCLUDE / "fkc_capi.h", CORE_LIB])):
+        return out
+    libdir = Path(torch.__file__).parent / "lib"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [
+        "g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+        f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_C",
+        "-DTORCH_API_INCLUDE_EXTENSION_H",
+        *[f"-I{p}" for p in cpp_extension.include_paths()],
+        f"-I{sysconfig.get_paths()['include']}", "-I/usr/local/cuda/include", f"-I{INCLUDE}",
+        str(src), "-o", str(out),
+        f"-L{libdir}", "-lc10", "-ltorch_cpu", "-ltorch", "-ltorch_python", "-lc10_cuda",
+        "-ltorch_cuda", f"-L{OUT_DIR}", "-lfkc_b200",
+        "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{libdir}",
+    ]
+    _run(cmd)
+    return out
+
+
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -134,6 +165,9 @@ def main(argv: list[str] | None = None) -> int:
         t = build_torch_api(force=args.force)
         if t is not None:
             print(f"built {t}")
+        m = build_py_module(force=args.force)
+        if m is not None:
+            print(f"built {m}")
     return 0
 
 

@@ -142,14 +142,14 @@ class MultimemLloyd:
     def __init__(self, x_local: torch.Tensor, n_clusters: int, n_max: int, group=None):
         import torch.distributed._symmetric_memory as symm
 
-        from . import _C
+        from . import _tensors
         from ._lib import lib
         from .kmeans import LloydState
 
         B, N, D = (int(v) for v in x_local.shape)
         K = int(n_clusters)
         dev = x_local.device
-        code = _C.dtype_code(x_local)
+        code = _tensors.dtype_code(x_local)
         es = x_local.element_size()
         ws_bytes = int(lib.fkc_lloyd_workspace_size(B, n_max, K, D, code))
 

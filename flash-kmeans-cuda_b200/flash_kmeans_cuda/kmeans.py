@@ -20,7 +20,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from . import _C, _lib
+from . import _lib, _tensors
 from ._trace import nvtx
 from ._lib import lib
 
@@ -44,13 +44,13 @@ class LloydState:
         self.device = x.device
         self.B, self.N, self.D = (int(s) for s in x.shape)
         self.K = int(n_clusters)
-        self.code = _C.dtype_code(x)
+        self.code = _tensors.dtype_code(x)
         dev = self.device
         with torch.cuda.device(dev):
             need = int(lib.fkc_lloyd_workspace_size(self.B, self.N, self.K, self.D, self.code))
             if ws is None:
                 self.ws_bytes = need
-                self.ws = _C.workspace(self.ws_bytes, dev)
+                self.ws = _tensors.workspace(self.ws_bytes, dev)
             else:
                 if ws.numel() < need:
                     raise RuntimeError(f"workspace needs {need} bytes (got {ws.numel()})")
@@ -66,7 +66,7 @@ class LloydState:
                                              self._stream()), "fkc_lloyd_prepare")
 
     def _stream(self) -> int:
-        return _C.stream_ptr(self.device)
+        return _tensors.stream_ptr(self.device)
 
     def _dims(self):
         return (self.B, self.N, self.K, self.D, self.code, self.ws.data_ptr(), self.ws_bytes,

@@ -31,7 +31,7 @@ from typing import List, Optional, Sequence, Tuple
 
 import torch
 
-from . import _C, _lib
+from . import _lib, _tensors
 from ._lib import lib
 
 _DEFAULT_BLOCK_BYTES = 256 << 20
@@ -59,10 +59,10 @@ class _Worker:
                  dtype: torch.dtype):
         self.device = device
         self.block_rows, self.K, self.D = block_rows, K, D
-        self.code = _C.dtype_code(torch.empty((), dtype=dtype))
+        self.code = _tensors.dtype_code(torch.empty((), dtype=dtype))
         with torch.cuda.device(device):
             self.ws_bytes = int(lib.fkc_lloyd_workspace_size(1, block_rows, K, D, self.code))
-            self.ws = _C.workspace(self.ws_bytes, device)
+            self.ws = _tensors.workspace(self.ws_bytes, device)
             self.x = [torch.empty((1, block_rows, D), dtype=dtype, device=device)
                       for _ in range(2)]
             self.ids = [torch.empty((1, block_rows), dtype=torch.int32, device=device)
@@ -245,7 +245,7 @@ def kmeans_largeN(
     plan = plan_blocks(N, block_rows, len(devs))
     pool = _Pool(devs, block_rows, K, D, x.dtype)
     ids_host = torch.empty((N,), dtype=torch.int32).pin_memory()
-    code = _C.dtype_code(x)
+    code = _tensors.dtype_code(x)
     c_next = torch.empty_like(c)
     shift = torch.zeros((1,), dtype=torch.float32, device=dev0)
     sums = torch.empty((1, K, D), dtype=torch.float32, device=dev0)
@@ -263,7 +263,7 @@ def kmeans_largeN(
                 counts.add_(w.counts.to(dev0, non_blocking=True))
             _lib.check(lib.fkc_finalize(sums.data_ptr(), counts.data_ptr(), c.data_ptr(),
                                         c_next.data_ptr(), None, shift.data_ptr(), 1, K, D,
-                                        code, _C.stream_ptr(dev0)), "fkc_finalize")
+                                        code, _tensors.stream_ptr(dev0)), "fkc_finalize")
             torch.cuda.synchronize(dev0)
         c, c_next = c_next, c
         n_run = it + 1

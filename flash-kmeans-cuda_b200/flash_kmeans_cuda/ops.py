@@ -13,7 +13,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from . import _C, _lib
+from . import _C, _lib, _tensors
 from ._lib import lib
 
 
@@ -75,14 +75,14 @@ def centroid_update_sorted(
         raise RuntimeError("sums_out and counts_out must be contiguous")
     if sums_out.numel() != B * K * D or counts_out.numel() != B * K:
         raise RuntimeError("sums_out must be (B, K, D) and counts_out (B, K)")
-    code = _C.dtype_code(x)
+    code = _tensors.dtype_code(x)
     with torch.cuda.device(x.device):
         ws_bytes = lib.fkc_update_workspace_size(B, N, K)
-        ws = _C.workspace(ws_bytes, x.device)
+        ws = _tensors.workspace(ws_bytes, x.device)
         _lib.check(
             lib.fkc_update(x.data_ptr(), cluster_ids.data_ptr(), sums_out.data_ptr(),
                            counts_out.data_ptr(), B, N, K, D, code, ws.data_ptr(), ws_bytes,
-                           _C.stream_ptr(x.device)),
+                           _tensors.stream_ptr(x.device)),
             "centroid_update_sorted")
     return sums_out, counts_out
 

@@ -20,6 +20,8 @@ def test_public_api_matches_reference_exports():
                               "centroid_update_sorted", "centroid_finalize"}
     from flash_kmeans_cuda import _C
 
+    # a compiled extension module, like the reference's nanobind _C
+    assert _C.__file__.endswith(".so")
     for name in ("euclid_assign", "centroid_update_sorted", "centroid_update_sorted_indexed",
                  "centroid_finalize"):
         assert callable(getattr(_C, name))
@@ -41,13 +43,22 @@ def test_kmeans_asserts_cuda_and_rank():
 
 
 def test_c_module_checks_like_torch_check():
-    from flash_kmeans_cuda import _C
+    from flash_kmeans_cuda import _C, _tensors
 
     x = torch.randn(1, 8, 16)
     with pytest.raises(RuntimeError, match="CUDA"):
         _C.euclid_assign(x, x[:, :2], torch.zeros(1, 8), torch.zeros(1, 2), None)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.euclid_assign(x, x[:, :2], torch.zeros(1, 8), torch.zeros(1, 2))  # out defaults to None
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.centroid_finalize(torch.zeros(1, 2, 16), torch.zeros(1, 2, dtype=torch.int32), x[:, :2])
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _C.centroid_update_sorted(x, torch.zeros(1, 8, dtype=torch.int32), torch.zeros(1, 2, 16),
+                                  torch.zeros(1, 2, dtype=torch.int32))
+    with pytest.raises(TypeError):
+        _C.euclid_assign(x, x[:, :2])  # missing arguments, as with the reference's module
     with pytest.raises(RuntimeError, match="unsupported dtype"):
-        _C.dtype_code(torch.zeros(1, dtype=torch.float64))
+        _tensors.dtype_code(torch.zeros(1, dtype=torch.float64))
 
 
 @pytest.mark.parametrize("total,world", [(10, 3), (524288, 8), (7, 8), (1, 2)])
