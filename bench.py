@@ -448,7 +448,7 @@ def run_reference_arm(args, w: dict) -> None:
 # --------------------------------------------------------------------- our arm
 def run_ours(args, w: dict) -> None:
     import flash_kmeans_cuda as fkc
-    from flash_kmeans_cuda import _C, _lib
+    from flash_kmeans_cuda import _lib
     from flash_kmeans_cuda.distributed import (MultimemLloyd, allreduce_sums_counts,
                                                batch_kmeans_Euclid_sharded, multimem_enabled,
                                                shard_bounds)
