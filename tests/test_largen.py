@@ -33,3 +33,12 @@ def test_host_x_checks():
         _check_host_x(torch.zeros((2, 8, 16), dtype=torch.float16))
     with pytest.raises(ValueError, match="dtype"):
         _check_host_x(torch.zeros((8, 16), dtype=torch.float64))
+
+
+def test_host_input_rejects_bad_x():
+    from flash_kmeans_cuda.largen import batch_kmeans_Euclid_host
+
+    with pytest.raises(ValueError, match="host memory"):
+        batch_kmeans_Euclid_host(torch.zeros(8, 4), 2)  # not (B, N, D)
+    with pytest.raises(ValueError):
+        batch_kmeans_Euclid_host(torch.zeros(1, 8, 4), 0)

@@ -69,3 +69,96 @@ def test_streamed_tol_and_default_blocks(cuda_device):
     assert c.shape == (50, 64) and c.dtype == x.dtype and c.is_cuda
     with pytest.raises(ValueError):
         kmeans_largeN(x.cuda(), 50, max_iters=1, devices=[0])
+
+
+ULP = {"float16": 2.0 ** -10, "bfloat16": 2.0 ** -7, "float32": 2.0 ** -23}
+
+
+@pytest.mark.parametrize("dtype,B,N,K,D,block_rows", [
+    ("float16", 1, 50000, 300, 128, 7168),   # 7 blocks, the last one shorter
+    ("bfloat16", 4, 9000, 200, 64, 4096),     # blocks inside every batch element
+    ("float32", 1, 20000, 256, 128, 65536),   # split fp32 rows, one block
+    ("float16", 1, 30000, 500, 384, 8192),    # CTA pairs
+])
+def test_host_input_first_iteration_matches(cuda_device, dtype, B, N, K, D, block_rows):
+    """One iteration from pinned host x (copy overlapped, per-block accumulate): labels
+    equal to batch_kmeans_Euclid's, centroids within the fp32 summation-order error."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+    from flash_kmeans_cuda.largen import batch_kmeans_Euclid_host
+
+    x = mixture(B, N, D, K, seed=N + K, zipf=1.1, dtype=dtype)
+    init = subset_init(x, K, seed=3)
+    ids_h, c_h, n_h = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=1,
+                                               init_centroids=init.pin_memory(),
+                                               block_rows=block_rows, overlap=True)
+    ids_r, c_r, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=1, init_centroids=init.cuda())
+    torch.cuda.synchronize()
+    assert n_h == n_r == 1 and ids_h.is_cuda and c_h.dtype == x.dtype
+    assert torch.equal(ids_h, ids_r)
+    # both against the float64 update of the same labels
+    xn, ids = to_np(x), ids_h.cpu().numpy()
+    s_ref, c_ref = orc.update(xn, ids, K)
+    fin = orc.finalize(s_ref, c_ref, to_np(init), dtype)
+    s_abs, _ = orc.update(np.abs(xn), ids, K)
+    mean_abs = s_abs / np.maximum(c_ref, 1)[..., None]
+    for got in (c_h, c_r):
+        err = np.abs(to_np(got) - fin)
+        assert (err <= 2 * ULP[dtype] * np.abs(fin) + 1e-5 * mean_abs + 1e-6).all()
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_host_input_free_running(cuda_device, dtype):
+    """Ten iterations from pinned host x against the device-resident loop: same iteration
+    count, labels >= 99.9% equal, final inertia within 0.05%."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+    from flash_kmeans_cuda.largen import batch_kmeans_Euclid_host
+
+    B, N, K, D = 1, 60000, 400, 128
+    x = mixture(B, N, D, K, seed=91, dtype=dtype)
+    init = subset_init(x, K, seed=92)
+    ids_h, c_h, n_h = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=10,
+                                               init_centroids=init, block_rows=16384,
+                                               overlap=True)
+    ids_r, c_r, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=10, init_centroids=init.cuda())
+    torch.cuda.synchronize()
+    assert n_h == n_r == 10
+    agree = (ids_h == ids_r).double().mean().item()
+    assert agree >= 0.999, agree
+    xn = to_np(x)
+    inert = lambda ids, c: float(((xn[0] - to_np(c)[0][ids.cpu().numpy()[0]]) ** 2).sum())
+    i_h, i_r = inert(ids_h, c_h), inert(ids_r, c_r)
+    assert abs(i_h - i_r) <= 5e-4 * i_r
+
+
+def test_host_input_tol_and_zero_iterations(cuda_device):
+    """tol stops like batch_kmeans_Euclid (also after the first, block-wise iteration);
+    max_iters=0 returns the initial centroids."""
+    from flash_kmeans_cuda import batch_kmeans_Euclid
+    from flash_kmeans_cuda.largen import batch_kmeans_Euclid_host
+
+    B, N, K, D = 1, 20000, 64, 64
+    x = mixture(B, N, D, K, seed=5, dtype="float16")
+    init = subset_init(x, K, seed=6)
+    # a huge tol stops after the first iteration on both paths
+    _, _, n_h = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=20, tol=1e9,
+                                         init_centroids=init, overlap=True)
+    _, _, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=20, tol=1e9,
+                                    init_centroids=init.cuda())
+    assert n_h == n_r == 1
+    # a moderate tol: both converge within a few iterations (counts may differ by one on a
+    # shift right at the threshold; the mixture converges quickly, so both stop early)
+    _, _, n_h = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=50, tol=1e-3,
+                                         init_centroids=init, overlap=True)
+    _, _, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=50, tol=1e-3,
+                                    init_centroids=init.cuda())
+    assert 1 <= n_h < 50 and abs(n_h - n_r) <= 1
+    ids0, c0, n0 = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=0, init_centroids=init)
+    torch.cuda.synchronize()
+    assert n0 == 0 and torch.equal(c0.cpu(), init)
+    # the copy-first route (chosen by size for small problems) gives the resident results
+    ids_c, c_c, n_c = batch_kmeans_Euclid_host(x.pin_memory(), K, max_iters=3,
+                                               init_centroids=init)
+    ids_r, c_r, n_r = batch_kmeans_Euclid(x.cuda(), K, max_iters=3, init_centroids=init.cuda())
+    torch.cuda.synchronize()
+    assert n_c == n_r == 3
+    assert (ids_c == ids_r).double().mean().item() >= 0.999  # fp32 sums: atomics order
