@@ -123,6 +123,56 @@ class LloydState:
                                           *self._dims()), "fkc_lloyd_iter")
 
 
+def _can_skip_x_sq_for_assign(x: torch.Tensor, n_clusters: int) -> bool:
+    """True when the assignment of ``x`` never reads ``x_sq`` (the reference's helper of
+    the same name, kmeans.py:48-70, answers it for its D=128 raw path). Here the
+    tensor-core route computes its own row norms: fp16/bf16 with D % 16 == 0 and D <= 512,
+    fp32 with D % 16 == 0 and D <= 256, unless FKC_ASSIGN_FORCE_SAFE=1 selects the
+    CUDA-core kernel (which reads x_sq). ``n_clusters`` does not matter here."""
+    del n_clusters
+    import os
+
+    if os.environ.get("FKC_ASSIGN_FORCE_SAFE", "") in ("1", "true"):
+        return False
+    D = int(x.shape[-1])
+    if D < 16 or D % 16 != 0:
+        return False
+    if x.dtype in (torch.float16, torch.bfloat16):
+        return D <= 512
+    return x.dtype == torch.float32 and D <= 256
+
+
+def _euclid_iter(
+    x: torch.Tensor,
+    x_sq: torch.Tensor,
+    centroids: torch.Tensor,
+    *,
+    compute_shift: bool = True,
+    cluster_ids_buf: Optional[torch.Tensor] = None,
+    sums_buf: Optional[torch.Tensor] = None,
+    counts_buf: Optional[torch.Tensor] = None,
+    new_centroids_buf: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, Optional[torch.Tensor], torch.Tensor]:
+    """One assign + update + finalize step through the public ops (the reference's
+    helper of the same name and contract, kmeans.py:73-105): returns
+    ``(new_centroids, shift, cluster_ids)``, ``shift`` the max over centroids of
+    ||new - old|| as a 0-d fp32 tensor, or None without ``compute_shift``. The
+    ``*_buf`` arguments are written in place when given. ``batch_kmeans_Euclid`` does not
+    use it: its loop runs as one CUDA graph over the fused iteration."""
+    from .ops import centroid_finalize, centroid_update_sorted, euclid_assign
+
+    B, K, D = centroids.shape
+    c_sq = (centroids.float() ** 2).sum(dim=-1).contiguous()
+    cluster_ids = euclid_assign(x, centroids, x_sq, c_sq=c_sq, out=cluster_ids_buf)
+    sums, counts = centroid_update_sorted(x, cluster_ids, K, sums_out=sums_buf,
+                                          counts_out=counts_buf)
+    new_centroids = centroid_finalize(sums, counts, centroids, out=new_centroids_buf)
+    shift = None
+    if compute_shift:
+        shift = (new_centroids.float() - centroids.float()).norm(dim=-1).max()
+    return new_centroids, shift, cluster_ids
+
+
 def init_centroids_random(x: torch.Tensor, n_clusters: int) -> torch.Tensor:
     """K random points per batch element, drawn WITH replacement (kmeans.py:153-157)."""
     B, N, D = x.shape

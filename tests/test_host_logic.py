@@ -94,3 +94,23 @@ def test_nvtx_ranges_are_noops_unless_enabled(monkeypatch):
     with pytest.raises(ZeroDivisionError):
         with _trace.nvtx("z"):
             1 / 0  # the range is popped on the way out
+
+
+def test_iteration_helpers_keep_the_reference_signatures():
+    """kmeans._euclid_iter / _can_skip_x_sq_for_assign (reference kmeans.py:48-105)."""
+    import inspect
+
+    from flash_kmeans_cuda import kmeans
+
+    sig = inspect.signature(kmeans._euclid_iter)
+    assert list(sig.parameters)[:3] == ["x", "x_sq", "centroids"]
+    for name in ("compute_shift", "cluster_ids_buf", "sums_buf", "counts_buf",
+                 "new_centroids_buf"):
+        assert sig.parameters[name].kind is inspect.Parameter.KEYWORD_ONLY
+    skip = kmeans._can_skip_x_sq_for_assign
+    assert skip(torch.zeros(1, 4, 128, dtype=torch.float16), 8)
+    assert skip(torch.zeros(1, 4, 512, dtype=torch.bfloat16), 8)
+    assert skip(torch.zeros(1, 4, 256, dtype=torch.float32), 8)
+    assert not skip(torch.zeros(1, 4, 384, dtype=torch.float32), 8)  # CUDA-core kernel
+    assert not skip(torch.zeros(1, 4, 100, dtype=torch.float16), 8)  # D % 16 != 0
+    assert not skip(torch.zeros(1, 4, 640, dtype=torch.float16), 8)  # D > 512

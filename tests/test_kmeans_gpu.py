@@ -297,3 +297,36 @@ def test_graph_loop_replay_and_edges(cuda_device):
     c = init.clone()
     assert int(st.run(c, 50, 1e30).item()) == 1  # every shift is below tol: one iteration
     _lib.device_status()
+
+
+@pytest.mark.parametrize("dtype", ["float16", "float32"])
+def test_euclid_iter_helper(cuda_device, dtype):
+    """kmeans._euclid_iter (the reference's one-step helper) against the float64 oracle,
+    with and without caller buffers."""
+    from flash_kmeans_cuda.kmeans import _euclid_iter
+
+    B, N, K, D = 2, 5000, 64, 128
+    x = mixture(B, N, D, K, seed=17, dtype=dtype)
+    c = subset_init(x, K, seed=18)
+    xd, cd = x.cuda(), c.cuda()
+    x_sq = (xd.float() ** 2).sum(-1)
+    new_c, shift, ids = _euclid_iter(xd, x_sq, cd)
+    torch.cuda.synchronize()
+    xn, cn = to_np(x), to_np(c)
+    ref = orc.assign(xn, cn)
+    got = ids.cpu().numpy()
+    assert not ((got != ref.ids) & ref.gap_mask()).any()
+    s_ref, c_ref = orc.update(xn, got, K)
+    fin = orc.finalize(s_ref, c_ref, cn, dtype)
+    _close_centroids(to_np(new_c), fin, dtype)
+    assert abs(float(shift) - orc.shift(to_np(new_c), cn)) <= 1e-5 + 1e-5 * float(shift)
+    # caller buffers are written in place and returned; no shift without compute_shift
+    bufs = dict(cluster_ids_buf=torch.empty_like(ids), sums_buf=torch.empty(
+        B, K, D, device="cuda"), counts_buf=torch.empty(B, K, dtype=torch.int32, device="cuda"),
+        new_centroids_buf=torch.empty_like(cd))
+    nc2, sh2, ids2 = _euclid_iter(xd, x_sq, cd, compute_shift=False, **bufs)
+    torch.cuda.synchronize()
+    assert sh2 is None
+    assert nc2.data_ptr() == bufs["new_centroids_buf"].data_ptr()
+    assert ids2.data_ptr() == bufs["cluster_ids_buf"].data_ptr()
+    assert torch.equal(ids2, ids)
