@@ -14,9 +14,10 @@
 //     row;
 //   * the accumulator gives each warp 64 sorted positions and splits them into
 //     32/L contiguous row streams, L = lanes per row (a D=128 fp16 row is 16
-//     lanes x 16 B). Each stream keeps P rows in flight (16-byte non-allocating
-//     loads), accumulates in registers and flushes every run with 16-byte
-//     vector atomics (red.global.add.v4.f32). No sorted copy of x is written.
+//     lanes x 16 B). Each stream keeps P rows in flight (16-byte cp.async copies
+//     into a per-warp shared-memory ring), accumulates in registers and flushes
+//     every run with 16-byte vector atomics (red.global.add.v4.f32). No sorted
+//     copy of x is written.
 //   * the scatter kernel also zeroes the sums the accumulator adds into;
 //   * with at most 32 rows per cluster on average, a single-GPU Lloyd step
 //     replaces accumulate + finalize by one pass over the clusters
@@ -336,19 +337,24 @@ __device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint
 // consecutive positions of one batch row (a multiple of 64, about equal spans
 // for all resident warps) and walks it in segments of 64 positions. A segment
 // is split into 32/L row streams of R = 2L consecutive positions; lane i of
-// stream g holds 16-byte vector i of the stream's current row. The labels and
+// stream g handles 16-byte vector i of the stream's current row. The labels and
 // source rows of a segment sit in two registers per lane (position
 // g*R + h*L + i in register h of lane g*L + i), so each step needs one shuffle
 // per value; the next segment's are loaded while the current one is walked.
-// Every stream keeps P row loads in flight, across segment boundaries. Rows of
-// one label are summed in registers (a stream's positions are sorted, so its
-// runs are contiguous even across segments) and flushed with vector atomics
-// when the label changes. Labels outside [0,K), including the -1 of unwritten
+// Every stream keeps P rows in flight, across segment boundaries, in shared
+// memory: each lane copies its 16-byte vector of a row with cp.async into a
+// per-warp ring of P slots (one copy group per step, empty when the position
+// has no row) and reads it back once the oldest group has landed; a lane reads
+// only what it copied itself, so no barrier is needed. Rows of one label are
+// summed in registers (a stream's positions are sorted, so its runs are
+// contiguous even across segments) and flushed with vector atomics when the
+// label changes. Labels outside [0,K), including the -1 of unwritten
 // positions, load nothing and are never flushed.
-// Occupancy: 106 registers (2 CTAs per SM) at D = 128 fp16. Capped at 80
-// registers (3 CTAs per SM, small spills) it measured no faster at c3 (38.8 vs
-// 37.6 us per launch); a row-read probe reaches 30.7 us for the same 134 MB of
-// random 256-byte rows at 4 CTAs per SM without the run bookkeeping.
+// Measured at c3 (D = 128 fp16, P = 16, 2 CTAs per SM): the update phase 52 us
+// against 57.6 us with P = 8 rows in flight held in registers (106 registers,
+// 2 CTAs per SM; capped at 80 registers for 3 CTAs per SM that version was no
+// faster); a row-read probe reaches 30.7 us for the same 134 MB of random
+// 256-byte rows at 4 CTAs per SM without the run bookkeeping.
 template <typename T, int L, int P>
 __global__ void __launch_bounds__(256) gather_accumulate_kernel(
     const T* __restrict__ x, const int32_t* __restrict__ perm,
@@ -356,13 +362,15 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
     int32_t* __restrict__ counts, int N, int K, int spans_per_batch, int span_len,
     int64_t total_spans) {
   pdl_wait();
+  extern __shared__ uint4 gather_ring[];  // (warps, P, 32) 16-byte slots
   constexpr int kVec = 16 / sizeof(T);
-  constexpr int R = 2 * L;  // positions per stream per 64-position segment
+  constexpr int R = 2 * L;
   static_assert(32 % L == 0 && R % P == 0, "stream layout");
   const int lane = threadIdx.x & 31;
   const int g = lane / L;
   const int i = lane % L;
   const int D = L * kVec;
+  uint4* my_ring = gather_ring + (threadIdx.x >> 5) * (P * 32) + lane;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t sp = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
        sp < total_spans; sp += warps) {
@@ -380,7 +388,7 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
         int l = q < sp1 ? ids_sorted[rb + q] : -1;
         if (l >= K) l = -1;
         int sr = l >= 0 ? (perm ? perm[rb + q] : q) : 0;
-        if (sr < 0 || sr >= N) {  // a caller's bad row index reads nothing
+        if (sr < 0 || sr >= N) {
           l = -1;
           sr = 0;
         }
@@ -388,22 +396,27 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
         src[h] = sr;
       }
     };
-    // Value of position g*R + j of the current segment (j known at compile time).
     auto meta_at = [&](const int (&a)[2], int j) {
       return __shfl_sync(0xFFFFFFFFu, a[j / L], g * L + (j % L));
     };
-    auto load_row = [&](int src) {
-      return ld_stream_v4(xb + static_cast<size_t>(src) * D + i * kVec);
+    // One copy group per step (empty when the position has no row).
+    auto load_row = [&](int slot, int src, bool on) {
+      if (on) {
+        const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(my_ring + slot * 32));
+        const T* srcp = xb + static_cast<size_t>(src) * D + i * kVec;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(srcp)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     };
     int lab[2], src[2], labn[2], srcn[2];
     load_meta(sp0, lab, src);
-    int ring[P];  // labels of the rows in flight
-    uint4 buf[P];
+    int ring[P];
 #pragma unroll
     for (int j = 0; j < P; ++j) {
       ring[j] = meta_at(lab, j);
       const int sr = meta_at(src, j);
-      if (ring[j] >= 0) buf[j] = load_row(sr);
+      load_row(j, sr, ring[j] >= 0);
     }
     float acc[kVec];
 #pragma unroll
@@ -429,7 +442,7 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
 #pragma unroll
       for (int j = 0; j < R; ++j) {
         const int l = ring[j % P];
-        const int jn = j + P;  // the row whose load goes out at this step
+        const int jn = j + P;
         const int ln = jn < R ? meta_at(lab, jn) : meta_at(labn, jn - R);
         const int sn = jn < R ? meta_at(src, jn) : meta_at(srcn, jn - R);
         if (l != cur) {
@@ -439,12 +452,14 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
           cur = l;
           len = 0;
         }
+        // the oldest of the P groups in flight (this step's row) has landed
+        asm volatile("cp.async.wait_group %0;" ::"n"(P - 1) : "memory");
         if (l >= 0) {
-          add_vec<T>(acc, buf[j % P]);
+          add_vec<T>(acc, my_ring[(j % P) * 32]);
           ++len;
         }
         ring[j % P] = ln;
-        if (ln >= 0) buf[j % P] = load_row(sn);
+        load_row(j % P, sn, ln >= 0);
       }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -453,6 +468,7 @@ __global__ void __launch_bounds__(256) gather_accumulate_kernel(
       }
     }
     flush();
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no copy outlives the span's ring use
   }
 }
 
@@ -778,9 +794,9 @@ int grid_for(int64_t items, int per_block) {
 
 // Resident blocks of `kern` on this device (block size 256), for persistent grids.
 template <typename K>
-int resident_blocks(K kern) {
+int resident_blocks(K kern, size_t smem = 0) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess ||
       per_sm < 1) {
     cudaGetLastError();
     per_sm = 1;
@@ -792,14 +808,20 @@ template <typename T, int L>
 int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, float* sums,
                   int32_t* counts, int64_t B, int64_t N, int64_t K, cudaStream_t stream) {
   constexpr int R = 2 * L;
-  constexpr int P = R < 8 ? R : 8;
+  constexpr int P = R < 16 ? R : 16;  // rows in flight per stream
   auto kern = gather_accumulate_kernel<T, L, P>;
+  constexpr int kSmem = 8 * P * 32 * 16;  // 8 warps x P slots x 32 lanes x 16 bytes
+  static std::atomic<bool> smem_set{false};  // per process; every device takes the same value
+  if (!smem_set.load(std::memory_order_relaxed)) {
+    FKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+    smem_set.store(true, std::memory_order_relaxed);
+  }
   // Resident blocks (the same on every device of one model). Host threads
   // driving several GPUs may race on the first call: atomic, same value.
   static std::atomic<int> cap_cache{0};
   int cap = cap_cache.load(std::memory_order_relaxed);
   if (cap == 0) {
-    cap = resident_blocks(kern);
+    cap = resident_blocks(kern, kSmem);
     cap_cache.store(cap, std::memory_order_relaxed);
   }
   // About one span per resident warp (spans a multiple of 32 positions), so
@@ -811,7 +833,7 @@ int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, fl
   spans_per_batch = (N + span_len - 1) / span_len;
   const int64_t total = spans_per_batch * B;
   const int64_t blocks = std::min<int64_t>((total + 7) / 8, cap);
-  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, perm,
+  return launch_pdl(kern, dim3(static_cast<unsigned>(blocks)), dim3(256), kSmem, stream, x, perm,
                     ids_sorted, sums, counts, static_cast<int>(N), static_cast<int>(K),
                     static_cast<int>(spans_per_batch), static_cast<int>(span_len), total);
 }
