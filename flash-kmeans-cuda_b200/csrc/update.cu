@@ -811,10 +811,15 @@ int launch_gather(const T* x, const int32_t* perm, const int32_t* ids_sorted, fl
   constexpr int P = R < 16 ? R : 16;  // rows in flight per stream
   auto kern = gather_accumulate_kernel<T, L, P>;
   constexpr int kSmem = 8 * P * 32 * 16;  // 8 warps x P slots x 32 lanes x 16 bytes
-  static std::atomic<bool> smem_set{false};  // per process; every device takes the same value
-  if (!smem_set.load(std::memory_order_relaxed)) {
+  // The shared-memory opt-in is a property of the kernel in each device's
+  // context: set it once per device ordinal (every call beyond ordinal 63).
+  static std::atomic<uint64_t> smem_set{0};
+  int dev = 0;
+  FKC_CUDA_TRY(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (bit == 0 || (smem_set.load(std::memory_order_relaxed) & bit) == 0) {
     FKC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-    smem_set.store(true, std::memory_order_relaxed);
+    smem_set.fetch_or(bit, std::memory_order_relaxed);
   }
   // Resident blocks (the same on every device of one model). Host threads
   // driving several GPUs may race on the first call: atomic, same value.
