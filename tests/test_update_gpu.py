@@ -59,6 +59,22 @@ def test_update_counting_sort(cuda_device, dtype, B, N, K, D, zipf):
     _check_sums(s.cpu().numpy(), c.cpu().numpy(), to_np(x), ids.numpy(), K)
 
 
+@pytest.mark.parametrize("N,K,zipf", [
+    (700_000, 4096, 0.0),      # 2048-row scatter chunks
+    (1_300_000, 16384, 1.1),   # 4096-row chunks, the largest K with shared-memory ranks
+    (1_300_000, 16385, 1.1),   # the per-row atomic scatter just above it
+])
+def test_counting_sort_large_chunks(cuda_device, N, K, zipf):
+    """Scatter chunk sizes that only large N selects, with a dominant Zipf cluster."""
+    from flash_kmeans_cuda import centroid_update_sorted
+
+    x = iid(1, N, 4, seed=N, dtype="float32")
+    ids = _labels(1, N, K, seed=K, zipf=zipf)
+    s, c = centroid_update_sorted(x.cuda(), ids.cuda(), K)
+    torch.cuda.synchronize()
+    _check_sums(s.cpu().numpy(), c.cpu().numpy(), to_np(x), ids.numpy(), K)
+
+
 @pytest.mark.parametrize("D", [1, 7, 16, 31, 32, 64, 128, 257])
 def test_sorted_and_indexed_match(cuda_device, D):
     """Reference _C semantics: accumulate into pre-zeroed buffers from sorted runs."""
