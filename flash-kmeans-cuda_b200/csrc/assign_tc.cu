@@ -89,6 +89,8 @@ constexpr int kEpiWarpBegin = 2;
 constexpr int kParts = kEpiWarps / 4;          // column slices of an item
 constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
 constexpr int kMaxTcD = 512;  // D > 256 runs on CTA pairs (each CTA holds half a chunk)
+// Split fp32 rows ([hi | lo], 2 Dp bf16 elements) up to fp32 D = 384.
+constexpr int kMaxSplitRowElems = 768;
 // Split mode partials: 2 slots per CTA x rows of a tile x (f32 score, i32 index).
 constexpr int kSplitMaxCtas = 256;
 constexpr int kSplitMaxRows = 256;
@@ -97,9 +99,17 @@ constexpr size_t kSplitPartialBytes = size_t{2} * kSplitMaxCtas * kSplitMaxRows 
 template <int DB, int MT, int NC, int ST, int CG>
 struct Cfg {
   static constexpr int kNB = NC / CG;  // centroid rows of a chunk held by one CTA
-  static constexpr int kXSubBytes = DB * kRowsPerSub * kKBlockBytes;
+  // Split fp32 rows wider than 512 elements (fp32 D > 256) do not fit as a
+  // resident row tile next to the centroid stages. Then x is streamed: every
+  // stage holds one 64-element column block j of the item's x rows and
+  // centroids, both halves (x_hi, x_lo, c_hi, c_lo), and the row tile keeps
+  // only the norm slice.
+  static constexpr bool kXStream = DB > 8;
+  static constexpr int kXBlockBytes = kRowsPerSub * kKBlockBytes;
+  static constexpr int kXSubBytes = kXStream ? 0 : DB * kXBlockBytes;
   static constexpr int kCBlockBytes = kNB * kKBlockBytes;
-  static constexpr int kCStageBytes = DB * kCBlockBytes;
+  static constexpr int kCStageBytes =
+      kXStream ? 2 * kXBlockBytes + 2 * kCBlockBytes : DB * kCBlockBytes;
   static constexpr int kAextSubBytes = kRowsPerSub * kExtBytes;
   static constexpr int kCextStageBytes = kNB * kExtBytes;
   // Accumulator slots: all 512 TMEM columns, NC columns each (2 or 4 slots).
@@ -148,6 +158,8 @@ struct Cfg {
   static_assert(NC >= 128 || CG == 2, "64-centroid chunks only on CTA pairs (UMMA M = 256)");
   static_assert(kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
+  static_assert(!kXStream || (CG == 1 && MT == 1 && DB % 2 == 0),
+                "streamed x: single CTAs, one sub-tile, [hi | lo] rows of whole blocks");
 
   // x buffer xi = (tile buffer) * MT + sub-tile
   __device__ static uint32_t x_full(uint32_t base, int xi) { return base + kOffBar + 8 * xi; }
@@ -495,6 +507,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = (tile - b * tiles_per_batch) * rows_per_tile +
                        static_cast<int>(rank) * MT * kRowsPerSub;
       for (int ch = ch0; ok && ch < ch1; ++ch) {
+        if constexpr (C::kXStream) {
+          // The tile's norm slice first: the MMA waits for it before the item's
+          // first stage, and the stages below would fill the ring before it.
+          if (ch == ch0) {
+            const int xi = static_cast<int>(x_it % C::kXS);
+            const uint32_t xph = (x_it / C::kXS) & 1u;
+            if (!warp_wait(C::x_empty(sb, xi), xph ^ 1u, abort_flag, lane)) {
+              if (lane == 0) raise_abort(abort_flag, err, kErrProducerX);
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              mbar_arrive_expect_tx(C::x_full(sb, xi), C::kXTxBytes);
+              tma_load<CG>(sb + C::kOffAext + xi * C::kAextSubBytes, &tm_aext, C::x_full(sb, xi),
+                           0, row0, b);
+            }
+            __syncwarp();
+            x_last_ph[xi] = static_cast<int>(xph);
+          }
+          constexpr int PB = DB / 2;  // column blocks of one half
+          const int crow = ch * NC;
+          for (int j = 0; ok && j < PB; ++j) {
+            const int st = static_cast<int>(c_it % ST);
+            const uint32_t ph = (c_it / ST) & 1u;
+            if (!warp_wait(C::c_empty(sb, st), ph ^ 1u, abort_flag, lane)) {
+              if (lane == 0) raise_abort(abort_flag, err, kErrProducerC);
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              const uint32_t full = C::c_full(sb, st);
+              const uint32_t stage = sb + C::kOffC + st * C::kCStageBytes;
+              mbar_arrive_expect_tx(full, C::kCTxBytes);
+              tma_load<CG>(stage, &tm_x, full, j * kKBlockElems, row0, b);
+              tma_load<CG>(stage + C::kXBlockBytes, &tm_x, full, (j + PB) * kKBlockElems, row0,
+                           b);
+              tma_load<CG>(stage + 2 * C::kXBlockBytes, &tm_c, full, j * kKBlockElems, crow, b);
+              tma_load<CG>(stage + 2 * C::kXBlockBytes + C::kCBlockBytes, &tm_c, full,
+                           (j + PB) * kKBlockElems, crow, b);
+              tma_load<CG>(sb + C::kOffCext + st * C::kCextStageBytes, &tm_cext, full, 0, crow,
+                           b);
+            }
+            __syncwarp();
+            c_last_ph[st] = static_cast<int>(ph);
+            ++c_it;
+          }
+          continue;
+        }
         const int st = static_cast<int>(c_it % ST);
         const uint32_t ph = (c_it / ST) & 1u;
         if (!warp_wait(C::c_empty(sb, st), ph ^ 1u, abort_flag, lane)) {
@@ -570,6 +630,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tile, ch0, ch1;
       while (ok && seg.next(tile, ch0, ch1)) {
         for (int ch = ch0; ok && ch < ch1; ++ch) {
+          if constexpr (C::kXStream) {
+            // One item per chunk (one sub-tile): for each column block j the
+            // stage's x_hi.c_hi, x_hi.c_lo and x_lo.c_hi K steps, then the norm
+            // step with the last stage's centroid norm slice.
+            constexpr int PB = DB / 2;
+            const int xi = static_cast<int>(x_it % C::kXS);
+            if (ch == ch0 && !mbar_wait(C::x_full(sb, xi), (x_it / C::kXS) & 1u, abort_flag)) {
+              raise_abort(abort_flag, err, kErrMmaX);
+              ok = false;
+              break;
+            }
+            const uint32_t slot = item % C::kSlots;
+            if (!mbar_wait(C::acc_empty(sb, slot), ((item / C::kSlots) & 1u) ^ 1u, abort_flag)) {
+              raise_abort(abort_flag, err, kErrMmaAcc);
+              ok = false;
+              break;
+            }
+            const uint32_t d_tmem = tmem_base + slot * NC;
+            for (int j = 0; ok && j < PB; ++j) {
+              const int st = static_cast<int>(c_it % ST);
+              const uint32_t ph = (c_it / ST) & 1u;
+              if (!mbar_wait(C::c_full(sb, st), ph, abort_flag)) {
+                raise_abort(abort_flag, err, kErrMmaC);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t stage = sb + C::kOffC + st * C::kCStageBytes;
+              const uint32_t a_hi = umma_desc_lo(stage);
+              const uint32_t a_lo = umma_desc_lo(stage + C::kXBlockBytes);
+              const uint32_t b_hi = umma_desc_lo(stage + 2 * C::kXBlockBytes);
+              const uint32_t b_lo = umma_desc_lo(stage + 2 * C::kXBlockBytes + C::kCBlockBytes);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                if (j * 4 + ks < ksteps) {
+                  uint32_t accf = (j > 0 || ks > 0) ? 1u : 0u;
+                  asm volatile("" : "+r"(accf));
+                  const uint32_t o = ks * 2;  // 32 bytes per K step, in 16-byte units
+                  mma<CG>(d_tmem, umma_desc(a_hi + o, kHi128), umma_desc(b_hi + o, kHi128), idesc,
+                          accf);
+                  mma<CG>(d_tmem, umma_desc(a_hi + o, kHi128), umma_desc(b_lo + o, kHi128), idesc,
+                          1u);
+                  mma<CG>(d_tmem, umma_desc(a_lo + o, kHi128), umma_desc(b_hi + o, kHi128), idesc,
+                          1u);
+                }
+              }
+              if (j == PB - 1)
+                mma_norm<CG>(
+                    d_tmem,
+                    umma_desc(umma_desc_lo(sb + C::kOffAext + xi * C::kAextSubBytes), kHi32),
+                    umma_desc(umma_desc_lo(sb + C::kOffCext + st * C::kCextStageBytes), kHi32),
+                    idesc_ext);
+              mma_done<CG>(C::c_empty(sb, st));
+              ++c_it;
+            }
+            if (!ok) break;
+            mma_done<CG>(C::acc_full(sb, slot));
+            if (ch == ch1 - 1) mma_done<CG>(C::x_empty(sb, xi));
+            ++item;
+            continue;
+          }
           const int st = static_cast<int>(c_it % ST);
           const uint32_t ph = (c_it / ST) & 1u;
           if (!mbar_wait(C::c_full(sb, st), ph, abort_flag)) {
@@ -1083,7 +1204,10 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
       if (D <= 128) return FKC_TC_SPLIT(2, 2, 256, 2, 1);
       if (D <= 256) return FKC_TC_SPLIT(4, 1, 128, 2, 1);
       if (D <= 384) return FKC_TC_SPLIT(6, 1, 128, 2, 2);
-      return FKC_TC_SPLIT(8, 1, 64, 2, 2);
+      if (D <= 512) return FKC_TC_SPLIT(8, 1, 64, 2, 2);
+      // fp32 D in (256, 384]: x streamed with the centroid stages (Cfg::kXStream),
+      // three 68 KB stages of one column block each.
+      return D <= 640 ? FKC_TC_SPLIT(10, 1, 128, 3, 1) : FKC_TC_SPLIT(12, 1, 128, 3, 1);
     }
   }
   if (D > 384) {
@@ -1119,9 +1243,10 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
 
 size_t assign_splitk_bytes() { return kSplitPartialBytes; }
 
-bool assign_tc_supported(int64_t D, int dtype) {
+bool assign_tc_supported(int64_t D, int dtype, bool split_rows) {
   if (dtype != FKC_DTYPE_F16 && dtype != FKC_DTYPE_BF16) return false;
-  if (D < 16 || D > kMaxTcD || D % 16 != 0) return false;
+  if (D < 16 || D % 16 != 0) return false;
+  if (D > (split_rows ? kMaxSplitRowElems : kMaxTcD)) return false;
   const DeviceInfo* di = nullptr;
   if (current_device_info(&di) != FKC_OK) return false;
   return di->cc_major == 10 && di->smem_optin >= static_cast<size_t>(kSmemLimit);
@@ -1130,15 +1255,15 @@ bool assign_tc_supported(int64_t D, int dtype) {
 int launch_assign_tc(const void* x, const void* centroids, const void* aext, const void* cext,
                      int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
                      int64_t K, int64_t D, int dtype, cudaStream_t stream, int split_d) {
-  FKC_REQUIRE(assign_tc_supported(D, dtype), "assign_tc: unsupported D=%lld / dtype=%d",
-              static_cast<long long>(D), dtype);
+  FKC_REQUIRE(assign_tc_supported(D, dtype, split_d > 0),
+              "assign_tc: unsupported D=%lld / dtype=%d", static_cast<long long>(D), dtype);
   FKC_REQUIRE(split_d == 0 || (dtype == FKC_DTYPE_BF16 && D % 128 == 0 && split_d % 16 == 0 &&
                                split_d > 0 && split_d <= D / 2),
               "assign_tc: bad split rows (D=%lld, split_d=%d)", static_cast<long long>(D),
               split_d);
   const bool bf16 = dtype == FKC_DTYPE_BF16;
-  // Split fp32 rows always run on single CTAs up to D = 256 (the pair choice
-  // applies to 16-bit inputs).
+  // The opt-in pair choice applies to 16-bit inputs; split fp32 rows take the
+  // configuration of their width (launch_tc_dispatch).
   const bool pairs = cta_group_choice() == 2 && split_d == 0;
   if (bf16)
     return pairs ? launch_tc_dispatch<true, 2>(x, centroids, aext, cext, ids, counts, splitk_ws,

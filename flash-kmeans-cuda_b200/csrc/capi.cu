@@ -146,10 +146,11 @@ namespace {
 
 // fp32 inputs on the tensor cores: x and the centroids are split into bf16
 // [hi | lo] rows of 2 Dp elements (Dp = D rounded up to 64; the kernel runs the
-// hi.hi, hi.lo and lo.hi passes, see launch_split_bf16), so 2 Dp must fit the
-// bf16 kernel (D <= 256).
+// hi.hi, hi.lo and lo.hi K steps, see launch_split_bf16). Up to D = 256 the
+// rows fit the bf16 kernel's resident row tile; up to D = 384 x is streamed
+// through the centroid stages.
 bool split_f32(int64_t D, int dtype) {
-  return dtype == FKC_DTYPE_F32 && D >= 16 && D <= 256 && D % 16 == 0;
+  return dtype == FKC_DTYPE_F32 && D >= 16 && D <= 384 && D % 16 == 0;
 }
 
 // Shape/dtype eligibility of the tensor-core assignment, independent of the
@@ -165,7 +166,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool use_tc(const void* x, const void* c, int64_t D, int dtype) {
   const bool split = split_f32(D, dtype);
   return tc_shape_ok(D, dtype) && !force_safe_path() && aligned16(x) && aligned16(c) &&
-         assign_tc_supported(split ? split_row_elems(D) : D, split ? FKC_DTYPE_BF16 : dtype);
+         assign_tc_supported(split ? split_row_elems(D) : D, split ? FKC_DTYPE_BF16 : dtype,
+                             split);
 }
 
 }  // namespace

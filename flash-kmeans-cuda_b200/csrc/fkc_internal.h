@@ -74,7 +74,9 @@ void count_launches(int n);
 
 // True when the tcgen05 assignment kernel handles this shape/dtype on the
 // current device.
-bool assign_tc_supported(int64_t D, int dtype);
+// split_rows: D is the width of split fp32 rows (launch_split_bf16), which
+// may exceed the 16-bit limit (x is then streamed through the stages).
+bool assign_tc_supported(int64_t D, int dtype, bool split_rows = false);
 // The host-only part of fkc_assign's route choice (no CUDA call): false when
 // the call certainly takes the CUDA-core kernel, which needs no workspace
 // (shape/dtype outside the tensor-core path, FKC_ASSIGN_FORCE_SAFE=1, or x /

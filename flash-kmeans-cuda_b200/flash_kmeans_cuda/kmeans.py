@@ -127,7 +127,7 @@ def _can_skip_x_sq_for_assign(x: torch.Tensor, n_clusters: int) -> bool:
     """True when the assignment of ``x`` never reads ``x_sq`` (the reference's helper of
     the same name, kmeans.py:48-70, answers it for its D=128 raw path). Here the
     tensor-core route computes its own row norms: fp16/bf16 with D % 16 == 0 and D <= 512,
-    fp32 with D % 16 == 0 and D <= 256, unless FKC_ASSIGN_FORCE_SAFE=1 selects the
+    fp32 with D % 16 == 0 and D <= 384, unless FKC_ASSIGN_FORCE_SAFE=1 selects the
     CUDA-core kernel (which reads x_sq). ``n_clusters`` does not matter here."""
     del n_clusters
     import os
@@ -139,7 +139,7 @@ def _can_skip_x_sq_for_assign(x: torch.Tensor, n_clusters: int) -> bool:
         return False
     if x.dtype in (torch.float16, torch.bfloat16):
         return D <= 512
-    return x.dtype == torch.float32 and D <= 256
+    return x.dtype == torch.float32 and D <= 384
 
 
 def _euclid_iter(

@@ -90,7 +90,7 @@ FKC_CAPI_EXPORT int fkc_selftest_wait_timeout(uint32_t timeout_us, fkc_stream_t 
  *   the reference's safe kernel does; the tensor-core path ignores it (as the
  *   reference's raw-distance mma path does).
  *   fp16/bf16 with D % 16 == 0 and D <= 512 run the tcgen05 kernel; so does
- *   fp32 with D % 16 == 0 and D <= 256 (x and c as split bf16 rows [hi | lo]
+ *   fp32 with D % 16 == 0 and D <= 384 (x and c as split bf16 rows [hi | lo]
  *   of 2 Dp elements, Dp = D rounded up to 64; the kernel accumulates hi.hi +
  *   hi.lo + lo.hi, ~2^-16 relative), when the workspace holds those rows
  *   (fkc_assign_workspace_size counts them); fp32 with a smaller or no

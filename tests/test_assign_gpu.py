@@ -137,16 +137,19 @@ def test_fp32_and_odd_d(cuda_device, B, N, K, D):
 
 
 @pytest.mark.parametrize("B,N,K,D", [(1, 3000, 500, 144), (2, 2000, 300, 192),
-                                     (1, 2500, 700, 256), (1, 1000, 100, 384)])
+                                     (1, 2500, 700, 256), (1, 3000, 260, 272),
+                                     (2, 1500, 333, 320), (1, 5000, 1000, 384),
+                                     (1, 1000, 100, 400)])
 def test_fp32_tensor_core_widths(cuda_device, B, N, K, D):
-    """fp32 up to D = 256 runs on the tensor cores as split bf16 rows ([hi | lo] halves,
-    three accumulating passes); D = 384 keeps the CUDA-core kernel. The assignment
-    workspace is non-zero exactly for the tensor-core route."""
+    """fp32 up to D = 384 runs on the tensor cores as split bf16 rows ([hi | lo] halves,
+    hi.hi + hi.lo + lo.hi K steps; above D = 256 x is streamed through the centroid
+    stages); D = 400 keeps the CUDA-core kernel. The assignment workspace is non-zero
+    exactly for the tensor-core route."""
     from flash_kmeans_cuda import _lib
 
     x = mixture(B, N, D, max(K // 4, 2), seed=N + D, dtype="float32")
     c = subset_init(x, K, seed=4)
-    assert (_lib.lib.fkc_assign_workspace_size(B, N, K, D, 2) > 0) == (D <= 256)
+    assert (_lib.lib.fkc_assign_workspace_size(B, N, K, D, 2) > 0) == (D <= 384)
     ids = _assign_gpu(x, c)
     _check(ids, orc.assign(to_np(x), to_np(c)), f"float32 D={D}")
 

@@ -77,7 +77,7 @@ def test_workspace_sizes_are_device_independent():
     # tensor-core shapes carry the norm-extension rows (32 B per point and per centroid)
     a = L.fkc_assign_workspace_size(1, 1000, 100, 128, 0)
     assert a >= 1000 * 32 + 100 * 32
-    # fp32 with D <= 256: plus the split bf16 operand rows ([hi | lo], 2 * Dp bf16 per point
+    # fp32 with D <= 384: plus the split bf16 operand rows ([hi | lo], 2 * Dp bf16 per point
     # and centroid, Dp = D rounded up to 64)
     al = lambda v: (v + 255) // 256 * 256
     assert L.fkc_assign_workspace_size(1, 1000, 100, 128, 2) == a + al(1000 * 256 * 2) + al(
@@ -85,7 +85,10 @@ def test_workspace_sizes_are_device_independent():
     a144 = L.fkc_assign_workspace_size(1, 1000, 100, 144, 0)
     assert L.fkc_assign_workspace_size(1, 1000, 100, 144, 2) == a144 + al(1000 * 384 * 2) + al(
         100 * 384 * 2)
-    assert L.fkc_assign_workspace_size(1, 1000, 100, 272, 2) == 0  # fp32, D > 256: CUDA cores
+    a272 = L.fkc_assign_workspace_size(1, 1000, 100, 272, 0)
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 272, 2) == a272 + al(1000 * 640 * 2) + al(
+        100 * 640 * 2)  # fp32, 256 < D <= 384: x streamed through the stages
+    assert L.fkc_assign_workspace_size(1, 1000, 100, 400, 2) == 0  # fp32, D > 384: CUDA cores
     assert L.fkc_assign_workspace_size(1, 1000, 100, 512, 1) > 0   # bf16 up to D = 512
     assert L.fkc_assign_workspace_size(1, 1000, 100, 528, 1) == 0
     assert L.fkc_assign_workspace_size(1, 1000, 100, 100, 0) == 0  # D % 16 != 0
@@ -202,9 +205,9 @@ def test_lloyd_entry_points_check_arguments_on_the_host():
 
 
 def test_fp32_workspace_grows_with_the_split_rows():
-    """fp32 rows of D <= 256 add 2 * Dp bf16 per point and per centroid to the Lloyd
+    """fp32 rows of D <= 384 add 2 * Dp bf16 per point and per centroid to the Lloyd
     workspace (the [hi | lo] split operands of the tensor-core path, Dp = D rounded up
-    to 64); D > 256 does not."""
+    to 64); D > 384 does not."""
     from flash_kmeans_cuda import _lib
 
     L = _lib.lib
@@ -219,4 +222,7 @@ def test_fp32_workspace_grows_with_the_split_rows():
     assert f32 - f16 == al(5000 * 128 * 2) + al(300 * 128 * 2)
     w272_16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 272, 0)
     w272_32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 272, 2)
-    assert w272_32 < w272_16  # fp32 D=272: no tensor-core rows at all
+    assert w272_32 >= w272_16 + al(5000 * 640 * 2) + al(300 * 640 * 2)  # Dp = 320
+    w400_16 = L.fkc_lloyd_workspace_size(1, 5000, 300, 400, 0)
+    w400_32 = L.fkc_lloyd_workspace_size(1, 5000, 300, 400, 2)
+    assert w400_32 < w400_16  # fp32 D=400: no tensor-core rows at all

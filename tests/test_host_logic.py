@@ -111,6 +111,7 @@ def test_iteration_helpers_keep_the_reference_signatures():
     assert skip(torch.zeros(1, 4, 128, dtype=torch.float16), 8)
     assert skip(torch.zeros(1, 4, 512, dtype=torch.bfloat16), 8)
     assert skip(torch.zeros(1, 4, 256, dtype=torch.float32), 8)
-    assert not skip(torch.zeros(1, 4, 384, dtype=torch.float32), 8)  # CUDA-core kernel
+    assert skip(torch.zeros(1, 4, 384, dtype=torch.float32), 8)  # x streamed with the stages
+    assert not skip(torch.zeros(1, 4, 400, dtype=torch.float32), 8)  # CUDA-core kernel
     assert not skip(torch.zeros(1, 4, 100, dtype=torch.float16), 8)  # D % 16 != 0
     assert not skip(torch.zeros(1, 4, 640, dtype=torch.float16), 8)  # D > 512

@@ -123,7 +123,50 @@ def slice_warp(B, segs, MT, slots, part):
         yield from finish()
 
 
-def run_cta(segs, MT, ST, NC, XS, own, nchunks, acc_empty_count=None):
+def producer_xs(B, segs, ST, XS, PB, norm_first=True):
+    """Streamed x (split fp32 rows wider than 512 elements, MT = 1): per tile the norm
+    slice into the row-tile buffer, then per chunk PB stages of one column block each."""
+    c_it = x_it = 0
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            if ch == ch0 and norm_first:
+                xi, xph = x_it % XS, (x_it // XS) & 1
+                yield from wait(B["x_empty"][xi], xph ^ 1)
+                B["x_full"][xi].arrive()
+            for j in range(PB):
+                st, ph = c_it % ST, (c_it // ST) & 1
+                yield from wait(B["c_empty"][st], ph ^ 1)
+                B["c_full"][st].arrive()
+                c_it += 1
+            if ch == ch0 and not norm_first:
+                xi, xph = x_it % XS, (x_it // XS) & 1
+                yield from wait(B["x_empty"][xi], xph ^ 1)
+                B["x_full"][xi].arrive()
+        x_it += 1
+
+
+def mma_xs(B, segs, ST, XS, slots, PB):
+    c_it = x_it = item = 0
+    for tile, ch0, ch1 in segs:
+        for ch in range(ch0, ch1):
+            xi = x_it % XS
+            if ch == ch0:
+                yield from wait(B["x_full"][xi], (x_it // XS) & 1)
+            slot = item % slots
+            yield from wait(B["acc_empty"][slot], ((item // slots) & 1) ^ 1)
+            for j in range(PB):
+                st, ph = c_it % ST, (c_it // ST) & 1
+                yield from wait(B["c_full"][st], ph)
+                B["c_empty"][st].arrive()
+                c_it += 1
+            B["acc_full"][slot].arrive()
+            if ch == ch1 - 1:
+                B["x_empty"][xi].arrive()
+            item += 1
+        x_it += 1
+
+
+def run_cta(segs, MT, ST, NC, XS, own, nchunks, acc_empty_count=None, PB=0, norm_first=True):
     slots = 512 // NC
     if acc_empty_count is None:
         acc_empty_count = 4 if own else 8
@@ -134,7 +177,10 @@ def run_cta(segs, MT, ST, NC, XS, own, nchunks, acc_empty_count=None):
         "acc_empty": [Bar(acc_empty_count) for _ in range(slots)],
         "merge_full": [Bar(4) for _ in range(2)], "merge_empty": [Bar(4) for _ in range(2)],
     }
-    roles = [producer(B, segs, MT, ST, XS, nchunks), mma(B, segs, MT, ST, XS, slots)]
+    if PB:
+        roles = [producer_xs(B, segs, ST, XS, PB, norm_first), mma_xs(B, segs, ST, XS, slots, PB)]
+    else:
+        roles = [producer(B, segs, MT, ST, XS, nchunks), mma(B, segs, MT, ST, XS, slots)]
     for w in range(8):  # epilogue warps 2..9: half = (w >> 2)
         part = w >> 2
         roles.append(owner_warp(B, segs, MT, slots, part) if own
@@ -167,6 +213,9 @@ CONFIGS = [
     dict(MT=2, NC=128, ST=2, XS=1, own=True),
     # D <= 256 (MT = 1): column slices, slice 1 sends, slice 0 finishes
     dict(MT=1, NC=128, ST=2, XS=1, own=False),
+    # split fp32, 256 < D <= 384: x streamed, five or six column blocks per item
+    dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=5),
+    dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=6),
 ]
 
 
@@ -180,6 +229,15 @@ def test_no_deadlock(cfg, total_tiles, nchunks, units):
         run_cta(whole, nchunks=nchunks, **cfg)
         if total_tiles * nchunks >= units:
             run_cta(segments(unit, units, total_tiles, nchunks), nchunks=nchunks, **cfg)
+
+
+def test_streamed_x_needs_the_norm_slice_first():
+    # the tile's norm slice requested after the chunk's stages: with more column blocks
+    # than stages the producer waits for a stage the MMA cannot free (it waits for the
+    # norm slice first), which the kernel avoids by loading the norm slice first
+    with pytest.raises(AssertionError, match="deadlock"):
+        run_cta([(0, 0, 2), (1, 0, 2)], MT=1, ST=3, NC=128, XS=2, own=False, nchunks=2, PB=6,
+                norm_first=False)
 
 
 def test_simulator_detects_a_broken_protocol():
