@@ -96,15 +96,15 @@ constexpr int kSplitMaxCtas = 256;
 constexpr int kSplitMaxRows = 256;
 constexpr size_t kSplitPartialBytes = size_t{2} * kSplitMaxCtas * kSplitMaxRows * 8;
 
-template <int DB, int MT, int NC, int ST, int CG>
+template <int DB, int MT, int NC, int ST, int CG, bool XST>
 struct Cfg {
   static constexpr int kNB = NC / CG;  // centroid rows of a chunk held by one CTA
-  // Split fp32 rows wider than 512 elements (fp32 D > 256) do not fit as a
-  // resident row tile next to the centroid stages. Then x is streamed: every
-  // stage holds one 64-element column block j of the item's x rows and
-  // centroids, both halves (x_hi, x_lo, c_hi, c_lo), and the row tile keeps
-  // only the norm slice.
-  static constexpr bool kXStream = DB > 8;
+  // XST (split fp32 rows): x is streamed with the centroid chunks instead of
+  // held as a resident row tile. Every stage holds one 64-element column block
+  // j of the item's x rows and centroids, both halves (x_hi, x_lo, c_hi,
+  // c_lo), and the row tile keeps only the norm slice. Rows wider than 512
+  // elements (fp32 D > 256) fit no other way.
+  static constexpr bool kXStream = XST;
   static constexpr int kXBlockBytes = kRowsPerSub * kKBlockBytes;
   static constexpr int kXSubBytes = kXStream ? 0 : DB * kXBlockBytes;
   static constexpr int kCBlockBytes = kNB * kKBlockBytes;
@@ -160,6 +160,7 @@ struct Cfg {
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
   static_assert(!kXStream || (CG == 1 && MT == 1 && DB % 2 == 0),
                 "streamed x: single CTAs, one sub-tile, [hi | lo] rows of whole blocks");
+  static_assert(DB <= 8 || kXStream, "rows wider than 512 elements need streamed x");
 
   // x buffer xi = (tile buffer) * MT + sub-tile
   __device__ static uint32_t x_full(uint32_t base, int xi) { return base + kOffBar + 8 * xi; }
@@ -408,7 +409,7 @@ struct SegIter {
   }
 };
 
-template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, bool XST>
 __global__ void __launch_bounds__(kThreads, 1)
     assign_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_aext,
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      int32_t* __restrict__ counts, int N, int K, int ksteps,
                      int tiles_per_batch, int total_tiles, float* __restrict__ partial_val,
                      int* __restrict__ partial_idx, int* __restrict__ err) {
-  using C = Cfg<DB, MT, NC, ST, CG>;
+  using C = Cfg<DB, MT, NC, ST, CG, XST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1084,12 +1085,12 @@ int cta_group_choice() {
 
 // D: elements per stored row (split fp32: 2 * Dp, the [hi | lo] halves);
 // ksteps: K steps of 16 elements per pass (D / 16, or the fp32 row's D / 16).
-template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, bool XST>
 int launch_tc_impl(const void* x, const void* centroids, const void* aext, const void* cext,
                    int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
                    int64_t K, int64_t D, int ksteps, cudaStream_t stream) {
-  using C = Cfg<DB, MT, NC, ST, CG>;
-  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG, SPLIT>;
+  using C = Cfg<DB, MT, NC, ST, CG, XST>;
+  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG, SPLIT, XST>;
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   FKC_CUDA_TRY(
@@ -1189,11 +1190,11 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
                        int64_t K, int64_t D, int split_d, cudaStream_t stream) {
   // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
 #define FKC_TC(DB_, MT_, NC_, ST_, CG_)                                                    \
-  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_, false>(                                    \
+  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_, false, false>(                             \
       x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
       static_cast<int>(D / 16), stream)
-#define FKC_TC_SPLIT(DB_, MT_, NC_, ST_, CG_)                                              \
-  launch_tc_impl<DB_, MT_, NC_, ST_, true, CG_, true>(                                     \
+#define FKC_TC_SPLIT(DB_, MT_, NC_, ST_, CG_, XST_)                                        \
+  launch_tc_impl<DB_, MT_, NC_, ST_, true, CG_, true, XST_>(                               \
       x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
       split_d / 16, stream)
   if constexpr (BF16 && CG == 1) {
@@ -1201,13 +1202,18 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
       // fp32 rows as [hi | lo] bf16 halves of Dp = D / 2 elements (a multiple of
       // 64): the configurations of a bf16 row of D = 2 Dp elements, each item
       // running three passes of split_d / 16 K steps.
-      if (D <= 128) return FKC_TC_SPLIT(2, 2, 256, 2, 1);
-      if (D <= 256) return FKC_TC_SPLIT(4, 1, 128, 2, 1);
-      if (D <= 384) return FKC_TC_SPLIT(6, 1, 128, 2, 2);
-      if (D <= 512) return FKC_TC_SPLIT(8, 1, 64, 2, 2);
-      // fp32 D in (256, 384]: x streamed with the centroid stages (Cfg::kXStream),
-      // three 68 KB stages of one column block each.
-      return D <= 640 ? FKC_TC_SPLIT(10, 1, 128, 3, 1) : FKC_TC_SPLIT(12, 1, 128, 3, 1);
+      if (D <= 128) return FKC_TC_SPLIT(2, 2, 256, 2, 1, false);
+      if (D <= 256) return FKC_TC_SPLIT(4, 1, 128, 2, 1, false);
+      if (D <= 384) return FKC_TC_SPLIT(6, 1, 128, 2, 2, false);
+      // Rows wider than 384 elements (fp32 D > 192): x streamed with the
+      // centroid stages (Cfg::kXStream), three 68 KB stages of one column block
+      // each. Measured at N=131072, K=2048: fp32 D=256 0.41 ms against 0.62 ms
+      // for CTA pairs holding [hi | lo] row tiles with 64-centroid chunks; at
+      // D=128 and D=192 the resident row tile is as fast or faster (0.235 /
+      // 0.324 ms against 0.235 / 0.328 streamed).
+      if (D <= 512) return FKC_TC_SPLIT(8, 1, 128, 3, 1, true);
+      return D <= 640 ? FKC_TC_SPLIT(10, 1, 128, 3, 1, true)
+                      : FKC_TC_SPLIT(12, 1, 128, 3, 1, true);
     }
   }
   if (D > 384) {

@@ -213,7 +213,8 @@ CONFIGS = [
     dict(MT=2, NC=128, ST=2, XS=1, own=True),
     # D <= 256 (MT = 1): column slices, slice 1 sends, slice 0 finishes
     dict(MT=1, NC=128, ST=2, XS=1, own=False),
-    # split fp32, 256 < D <= 384: x streamed, five or six column blocks per item
+    # split fp32, 192 < D <= 384: x streamed, four to six column blocks per item
+    dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=4),
     dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=5),
     dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=6),
 ]
@@ -314,7 +315,7 @@ def run_pair(segs, MT, ST, NC, XS, own, nchunks):
 
 
 PAIR_CONFIGS = [
-    dict(MT=1, NC=64, ST=2, XS=1, own=False),    # 384 < D <= 512 (and split fp32, D > 192)
+    dict(MT=1, NC=64, ST=2, XS=1, own=False),    # 384 < D <= 512
     dict(MT=1, NC=128, ST=2, XS=1, own=False),   # 256 < D <= 384
     dict(MT=2, NC=256, ST=8, XS=1, own=True),    # D <= 64 (pairs opted in)
     dict(MT=2, NC=256, ST=4, XS=1, own=False),   # D <= 128 (pairs opted in)
