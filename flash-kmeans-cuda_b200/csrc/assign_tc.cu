@@ -96,20 +96,21 @@ constexpr int kSplitMaxCtas = 256;
 constexpr int kSplitMaxRows = 256;
 constexpr size_t kSplitPartialBytes = size_t{2} * kSplitMaxCtas * kSplitMaxRows * 8;
 
-template <int DB, int MT, int NC, int ST, int CG, bool XST>
+template <int DB, int MT, int NC, int ST, int CG, int XSM>
 struct Cfg {
   static constexpr int kNB = NC / CG;  // centroid rows of a chunk held by one CTA
-  // XST (split fp32 rows): x is streamed with the centroid chunks instead of
-  // held as a resident row tile. Every stage holds one 64-element column block
-  // j of the item's x rows and centroids, both halves (x_hi, x_lo, c_hi,
-  // c_lo), and the row tile keeps only the norm slice. Rows wider than 512
-  // elements (fp32 D > 256) fit no other way.
-  static constexpr bool kXStream = XST;
+  // XSM != 0: x is streamed with the centroid chunks instead of held as a
+  // resident row tile. Every stage holds one 64-element column block j of the
+  // item's x rows and centroids (XSM = 2, split fp32 rows: both halves, x_hi,
+  // x_lo, c_hi, c_lo), and the row tile keeps only the norm slice. Rows wider
+  // than 512 elements (fp32 D > 256) fit no other way.
+  static constexpr bool kXStream = XSM != 0;
+  static constexpr int kHalves = XSM == 2 ? 2 : 1;
   static constexpr int kXBlockBytes = kRowsPerSub * kKBlockBytes;
   static constexpr int kXSubBytes = kXStream ? 0 : DB * kXBlockBytes;
   static constexpr int kCBlockBytes = kNB * kKBlockBytes;
   static constexpr int kCStageBytes =
-      kXStream ? 2 * kXBlockBytes + 2 * kCBlockBytes : DB * kCBlockBytes;
+      kXStream ? kHalves * (kXBlockBytes + kCBlockBytes) : DB * kCBlockBytes;
   static constexpr int kAextSubBytes = kRowsPerSub * kExtBytes;
   static constexpr int kCextStageBytes = kNB * kExtBytes;
   // Accumulator slots: all 512 TMEM columns, NC columns each (2 or 4 slots).
@@ -158,7 +159,7 @@ struct Cfg {
   static_assert(NC >= 128 || CG == 2, "64-centroid chunks only on CTA pairs (UMMA M = 256)");
   static_assert(kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kParts >= 2, "the merge handshake expects at least two column slices");
-  static_assert(!kXStream || (CG == 1 && MT == 1 && DB % 2 == 0),
+  static_assert(!kXStream || (CG == 1 && MT == 1 && DB % kHalves == 0),
                 "streamed x: single CTAs, one sub-tile, [hi | lo] rows of whole blocks");
   static_assert(DB <= 8 || kXStream, "rows wider than 512 elements need streamed x");
 
@@ -409,7 +410,7 @@ struct SegIter {
   }
 };
 
-template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, bool XST>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, int XSM>
 __global__ void __launch_bounds__(kThreads, 1)
     assign_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                      const __grid_constant__ CUtensorMap tm_aext,
@@ -418,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      int32_t* __restrict__ counts, int N, int K, int ksteps,
                      int tiles_per_batch, int total_tiles, float* __restrict__ partial_val,
                      int* __restrict__ partial_idx, int* __restrict__ err) {
-  using C = Cfg<DB, MT, NC, ST, CG, XST>;
+  using C = Cfg<DB, MT, NC, ST, CG, XSM>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -527,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             x_last_ph[xi] = static_cast<int>(xph);
           }
-          constexpr int PB = DB / 2;  // column blocks of one half
+          constexpr int PB = DB / C::kHalves;  // column blocks of one half
           const int crow = ch * NC;
           for (int j = 0; ok && j < PB; ++j) {
             const int st = static_cast<int>(c_it % ST);
@@ -540,13 +541,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
               const uint32_t full = C::c_full(sb, st);
               const uint32_t stage = sb + C::kOffC + st * C::kCStageBytes;
+              const uint32_t cblk = stage + C::kHalves * C::kXBlockBytes;
               mbar_arrive_expect_tx(full, C::kCTxBytes);
               tma_load<CG>(stage, &tm_x, full, j * kKBlockElems, row0, b);
-              tma_load<CG>(stage + C::kXBlockBytes, &tm_x, full, (j + PB) * kKBlockElems, row0,
-                           b);
-              tma_load<CG>(stage + 2 * C::kXBlockBytes, &tm_c, full, j * kKBlockElems, crow, b);
-              tma_load<CG>(stage + 2 * C::kXBlockBytes + C::kCBlockBytes, &tm_c, full,
-                           (j + PB) * kKBlockElems, crow, b);
+              tma_load<CG>(cblk, &tm_c, full, j * kKBlockElems, crow, b);
+              if constexpr (C::kHalves == 2) {
+                tma_load<CG>(stage + C::kXBlockBytes, &tm_x, full, (j + PB) * kKBlockElems,
+                             row0, b);
+                tma_load<CG>(cblk + C::kCBlockBytes, &tm_c, full, (j + PB) * kKBlockElems, crow,
+                             b);
+              }
               tma_load<CG>(sb + C::kOffCext + st * C::kCextStageBytes, &tm_cext, full, 0, crow,
                            b);
             }
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // One item per chunk (one sub-tile): for each column block j the
             // stage's x_hi.c_hi, x_hi.c_lo and x_lo.c_hi K steps, then the norm
             // step with the last stage's centroid norm slice.
-            constexpr int PB = DB / 2;
+            constexpr int PB = DB / C::kHalves;
             const int xi = static_cast<int>(x_it % C::kXS);
             if (ch == ch0 && !mbar_wait(C::x_full(sb, xi), (x_it / C::kXS) & 1u, abort_flag)) {
               raise_abort(abort_flag, err, kErrMmaX);
@@ -661,8 +665,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t stage = sb + C::kOffC + st * C::kCStageBytes;
               const uint32_t a_hi = umma_desc_lo(stage);
               const uint32_t a_lo = umma_desc_lo(stage + C::kXBlockBytes);
-              const uint32_t b_hi = umma_desc_lo(stage + 2 * C::kXBlockBytes);
-              const uint32_t b_lo = umma_desc_lo(stage + 2 * C::kXBlockBytes + C::kCBlockBytes);
+              const uint32_t b_hi = umma_desc_lo(stage + C::kHalves * C::kXBlockBytes);
+              const uint32_t b_lo =
+                  umma_desc_lo(stage + C::kHalves * C::kXBlockBytes + C::kCBlockBytes);
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks) {
                 if (j * 4 + ks < ksteps) {
@@ -671,10 +676,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const uint32_t o = ks * 2;  // 32 bytes per K step, in 16-byte units
                   mma<CG>(d_tmem, umma_desc(a_hi + o, kHi128), umma_desc(b_hi + o, kHi128), idesc,
                           accf);
-                  mma<CG>(d_tmem, umma_desc(a_hi + o, kHi128), umma_desc(b_lo + o, kHi128), idesc,
-                          1u);
-                  mma<CG>(d_tmem, umma_desc(a_lo + o, kHi128), umma_desc(b_hi + o, kHi128), idesc,
-                          1u);
+                  if constexpr (C::kHalves == 2) {
+                    mma<CG>(d_tmem, umma_desc(a_hi + o, kHi128), umma_desc(b_lo + o, kHi128),
+                            idesc, 1u);
+                    mma<CG>(d_tmem, umma_desc(a_lo + o, kHi128), umma_desc(b_hi + o, kHi128),
+                            idesc, 1u);
+                  }
                 }
               }
               if (j == PB - 1)
@@ -1085,12 +1092,12 @@ int cta_group_choice() {
 
 // D: elements per stored row (split fp32: 2 * Dp, the [hi | lo] halves);
 // ksteps: K steps of 16 elements per pass (D / 16, or the fp32 row's D / 16).
-template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, bool XST>
+template <int DB, int MT, int NC, int ST, bool BF16, int CG, bool SPLIT, int XSM>
 int launch_tc_impl(const void* x, const void* centroids, const void* aext, const void* cext,
                    int32_t* ids, int32_t* counts, void* splitk_ws, int64_t B, int64_t N,
                    int64_t K, int64_t D, int ksteps, cudaStream_t stream) {
-  using C = Cfg<DB, MT, NC, ST, CG, XST>;
-  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG, SPLIT, XST>;
+  using C = Cfg<DB, MT, NC, ST, CG, XSM>;
+  auto kern = assign_tc_kernel<DB, MT, NC, ST, BF16, CG, SPLIT, XSM>;
   const DeviceInfo* di = nullptr;
   FKC_TRY(current_device_info(&di));
   FKC_CUDA_TRY(
@@ -1190,11 +1197,11 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
                        int64_t K, int64_t D, int split_d, cudaStream_t stream) {
   // (DB, MT, NC, ST) per D so that x sub-tiles + ST centroid stages fit in 227 KB.
 #define FKC_TC(DB_, MT_, NC_, ST_, CG_)                                                    \
-  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_, false, false>(                             \
+  launch_tc_impl<DB_, MT_, NC_, ST_, BF16, CG_, false, 0>(                                 \
       x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
       static_cast<int>(D / 16), stream)
 #define FKC_TC_SPLIT(DB_, MT_, NC_, ST_, CG_, XST_)                                        \
-  launch_tc_impl<DB_, MT_, NC_, ST_, true, CG_, true, XST_>(                               \
+  launch_tc_impl<DB_, MT_, NC_, ST_, true, CG_, true, (XST_) ? 2 : 0>(                     \
       x, centroids, aext, cext, ids, counts, (CG_) == 1 ? splitk_ws : nullptr, B, N, K, D, \
       split_d / 16, stream)
   if constexpr (BF16 && CG == 1) {
@@ -1217,9 +1224,20 @@ int launch_tc_dispatch(const void* x, const void* centroids, const void* aext, c
     }
   }
   if (D > 384) {
-    // 384 < D <= 512: CTA pairs with 64-centroid chunks, each CTA holding 32
-    // centroid rows per stage (x 128 KB + 2 x 32 KB per CTA); an item is
-    // M = 256 x N = 64 x K = D, long enough that the MMA stream dominates.
+    if constexpr (CG == 1) {
+      // 384 < D <= 512: x streamed with 256-centroid chunks (three 56 KB stages
+      // of one 64-element column block of x and of the chunk each).
+      return D <= 448
+                 ? launch_tc_impl<7, 1, 256, 3, BF16, 1, false, 1>(
+                       x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
+                       static_cast<int>(D / 16), stream)
+                 : launch_tc_impl<8, 1, 256, 3, BF16, 1, false, 1>(
+                       x, centroids, aext, cext, ids, counts, splitk_ws, B, N, K, D,
+                       static_cast<int>(D / 16), stream);
+    }
+    // CTA pairs (opted in): 64-centroid chunks, each CTA holding 32 centroid
+    // rows per stage (x 128 KB + 2 x 32 KB per CTA); an item is M = 256 x
+    // N = 64 x K = D, long enough that the MMA stream dominates.
     return FKC_TC(8, 1, 64, 2, 2);
   }
   if (D > 256) {

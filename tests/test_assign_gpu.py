@@ -61,8 +61,10 @@ SHAPES = [
     (1, 2048, 4096, 128),
     (1, 1500, 300, 320),    # D > 256: CTA-pair kernel, 64 centroid rows per CTA
     (2, 3000, 700, 384),
-    (1, 2000, 500, 448),    # D > 384: CTA pairs with 64-centroid chunks, 32 rows per CTA
+    (1, 1200, 200, 400),    # D > 384: x streamed with the centroid stages (last block partial)
+    (1, 2000, 500, 448),
     (2, 1700, 333, 512),
+    (1, 70000, 600, 512),   # more row tiles than SMs (two x buffers in turn)
 ]
 
 

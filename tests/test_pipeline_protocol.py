@@ -217,6 +217,9 @@ CONFIGS = [
     dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=4),
     dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=5),
     dict(MT=1, NC=128, ST=3, XS=2, own=False, PB=6),
+    # fp16/bf16, 384 < D <= 512: x streamed with 256-centroid chunks, 7 or 8 blocks per item
+    dict(MT=1, NC=256, ST=3, XS=2, own=False, PB=7),
+    dict(MT=1, NC=256, ST=3, XS=2, own=False, PB=8),
 ]
 
 
@@ -315,7 +318,7 @@ def run_pair(segs, MT, ST, NC, XS, own, nchunks):
 
 
 PAIR_CONFIGS = [
-    dict(MT=1, NC=64, ST=2, XS=1, own=False),    # 384 < D <= 512
+    dict(MT=1, NC=64, ST=2, XS=1, own=False),    # 384 < D <= 512 (pairs opted in)
     dict(MT=1, NC=128, ST=2, XS=1, own=False),   # 256 < D <= 384
     dict(MT=2, NC=256, ST=8, XS=1, own=True),    # D <= 64 (pairs opted in)
     dict(MT=2, NC=256, ST=4, XS=1, own=False),   # D <= 128 (pairs opted in)
