@@ -41,9 +41,9 @@ def _close_centroids(got, ref, dtype, rel=1e-3):
     # shares tiles between CTAs (split mode) and merges them in a fixup pass
     (2, 10000, 700, 64, 0.0),
     (1, 9000, 2000, 128, 1.1),
-    (1, 6000, 300, 384, 0.0),  # D > 256 (CTA pairs)
+    (1, 6000, 300, 384, 0.0),  # D > 256: CTA pairs (fp32: split rows, x streamed)
     (1, 5000, 256, 512, 0.0),  # D = 512: x streamed with the stages (fp32: CUDA cores)
-    (1, 8000, 300, 256, 1.1),  # D = 256: fp32 as split [hi | lo] rows in three passes
+    (1, 8000, 300, 256, 1.1),  # D = 256: fp32 as split [hi | lo] rows, x streamed
     # small clusters on average (the fused update + finalize pass) with a few
     # hot ones split into 64-row units that the cluster's last unit finishes
     (2, 20000, 700, 64, 1.1),
