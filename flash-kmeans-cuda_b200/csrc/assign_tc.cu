@@ -88,7 +88,7 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // warp 0 TMA, warp 1 MMA, epilog
 constexpr int kEpiWarpBegin = 2;
 constexpr int kParts = kEpiWarps / 4;          // column slices of an item
 constexpr int kSmemLimit = 232448;             // 227 KB opt-in per block on sm_100
-constexpr int kMaxTcD = 512;  // D > 256 runs on CTA pairs (each CTA holds half a chunk)
+constexpr int kMaxTcD = 512;  // 256 < D <= 384 on CTA pairs, wider rows streamed
 // Split fp32 rows ([hi | lo], 2 Dp bf16 elements) up to fp32 D = 384.
 constexpr int kMaxSplitRowElems = 768;
 // Split mode partials: 2 slots per CTA x rows of a tile x (f32 score, i32 index).
@@ -637,8 +637,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ch = ch0; ok && ch < ch1; ++ch) {
           if constexpr (C::kXStream) {
             // One item per chunk (one sub-tile): for each column block j the
-            // stage's x_hi.c_hi, x_hi.c_lo and x_lo.c_hi K steps, then the norm
-            // step with the last stage's centroid norm slice.
+            // stage's x.c K steps (split rows: x_hi.c_hi, x_hi.c_lo and
+            // x_lo.c_hi), then the norm step with the last stage's centroid norm
+            // slice.
             constexpr int PB = DB / C::kHalves;
             const int xi = static_cast<int>(x_it % C::kXS);
             if (ch == ch0 && !mbar_wait(C::x_full(sb, xi), (x_it / C::kXS) & 1u, abort_flag)) {
